@@ -1,0 +1,353 @@
+"""candle_moe: Python mirror of the kozistr/candle-moe Rust API over the candle-moe-b200 C ABI.
+
+The reference crate exposes ``apply_topk_softmax_inplace``, ``Activation``, and
+``FusedMoE{num_experts, num_selected_experts, activation}`` with ``FusedMoE::new`` /
+``FusedMoE::forward`` (src/lib.rs:124-335).  This module keeps those names, argument meanings
+and error cases, with torch CUDA tensors in place of candle tensors, and calls the B200 kernels
+through ``libcandle_moe_b200.so`` (include/candle_moe.h).  There is no CPU path: when the shared
+library is missing, every call raises.
+
+Extensions beyond the reference API: ``topk_softmax`` (allocating, optional renormalisation),
+``route_prep`` (the sort/align step on its own), ``fused_moe`` (status-checked, optional
+caller workspace), ``workspace_size``, ``device_error_bits``, ``set_gemm_path`` /
+``last_gemm_path``.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+import os
+from typing import Optional
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcandle_moe_b200.so")
+_lib: Optional[ctypes.CDLL] = None
+
+MOE_OK, MOE_ERR_INVALID_ARG, MOE_ERR_UNSUPPORTED, MOE_ERR_CUDA, MOE_ERR_WORKSPACE, \
+    MOE_ERR_NO_MEMORY = range(6)
+
+
+class MoeError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {lib().moe_status_string(status).decode()} (status {status})")
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C-ABI library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python candle-moe_b200/build.py`; "
+                "candle_moe has no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        P, I32, I64, U32, SZ = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
+                                ctypes.c_size_t)
+        L.topk_softmax.argtypes = [P, P, P, P, I32, I32, I32, P]
+        L.topk_softmax.restype = None
+        L.fused_moe.argtypes = [P, P, P, P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_int, U32, U32, P]
+        L.fused_moe.restype = None
+        L.moe_last_status.argtypes = []
+        L.moe_last_status.restype = ctypes.c_int
+        L.moe_status_string.argtypes = [ctypes.c_int]
+        L.moe_status_string.restype = ctypes.c_char_p
+        L.moe_topk_softmax_v2.argtypes = [P, P, P, P, I32, I64, I32, I32, P]
+        L.moe_topk_softmax_v2.restype = ctypes.c_int
+        L.moe_route_prep.argtypes = [P, P, I64, I32, I32, P, P, P, P]
+        L.moe_route_prep.restype = ctypes.c_int
+        L.moe_fused_workspace_size.argtypes = [I64, I32, I32, I32, I32, U32, U32]
+        L.moe_fused_workspace_size.restype = SZ
+        L.moe_fused_v2.argtypes = [P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, U32, U32, P,
+                                   SZ, P]
+        L.moe_fused_v2.restype = ctypes.c_int
+        L.moe_device_error_bits.argtypes = [I32, I32]
+        L.moe_device_error_bits.restype = U32
+        L.moe_set_gemm_path.argtypes = [I32]
+        L.moe_set_gemm_path.restype = I32
+        L.moe_last_gemm_path.argtypes = []
+        L.moe_last_gemm_path.restype = I32
+        _lib = L
+    return _lib
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a cuda tensor")
+
+
+def _need_contig(t: torch.Tensor, name: str):
+    # The reference takes only the start offset of each tensor and ignores its strides
+    # (src/lib.rs:393-410), so a permuted view is silently misread there; here it is an error.
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous (row-major)")
+
+
+_INDEX_DTYPES = (torch.int32, getattr(torch, "uint32", torch.int32))
+
+
+# ---------------------------------------------------------------------------------------------
+# router: src/lib.rs:10-155
+# ---------------------------------------------------------------------------------------------
+
+def apply_topk_softmax_inplace(gating_output: torch.Tensor, topk_weight: torch.Tensor,
+                               topk_indices: torch.Tensor,
+                               token_expert_indices: torch.Tensor) -> None:
+    """Softmax over experts, then top-k, written into the three caller tensors
+    (src/lib.rs:124-155 -> kernels/topk_softmax.cu:331-353).
+
+    gating_output [T,E] f32; topk_weight [T,k] f32; topk_indices / token_expert_indices [T,k]
+    int32 or uint32.  E must be a power of two <= 256.  The reference dispatches on
+    topk_weight's dtype but its kernel always reads f32 (src/lib.rs:130-148 vs
+    topk_softmax.cu:344), so only f32 is accepted here."""
+    for t, n in ((gating_output, "gating_output"), (topk_weight, "topk_weight"),
+                 (topk_indices, "topk_indices"), (token_expert_indices, "token_expert_indices")):
+        _need_cuda(t, n)
+    if any(t.dim() != 2 for t in (gating_output, topk_weight, topk_indices, token_expert_indices)):
+        raise ValueError(
+            "apply_topk_softmax_inplace expects input tensors of rank 2 "
+            f"(w: {tuple(topk_weight.shape)}, i: {tuple(topk_indices.shape)}, "
+            f"ei: {tuple(token_expert_indices.shape)}, g: {tuple(gating_output.shape)})")
+    if topk_weight.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise TypeError("apply_topk_softmax_inplace is only supported for f32, f16 and bf16 "
+                        f"({topk_weight.dtype})")
+    if gating_output.dtype != torch.float32 or topk_weight.dtype != torch.float32:
+        raise TypeError("the router reads and writes f32 only (gating_output and topk_weight "
+                        "must be float32)")
+    if topk_indices.dtype not in _INDEX_DTYPES or token_expert_indices.dtype not in _INDEX_DTYPES:
+        raise TypeError("topk_indices and token_expert_indices must be int32 or uint32")
+    num_tokens, top_k = topk_weight.shape
+    num_experts = gating_output.shape[1]
+    if num_experts == 0 or (num_experts & (num_experts - 1)) != 0 or num_experts > 256:
+        raise ValueError("num_experts should be power of 2 and smaller than 256 "
+                         f"(num_experts: {num_experts})")
+    if tuple(topk_indices.shape) != (num_tokens, top_k):
+        raise ValueError(f"shape mismatch topk_indices {tuple(topk_indices.shape)}, expected "
+                         f"{(num_tokens, top_k)}")
+    if tuple(token_expert_indices.shape) != (num_tokens, top_k):
+        raise ValueError(f"shape mismatch token_expert_indices "
+                         f"{tuple(token_expert_indices.shape)}, expected {(num_tokens, top_k)}")
+    if gating_output.shape[0] != num_tokens:
+        raise ValueError("gating_output and topk_weight disagree on the number of tokens")
+    for t, n in ((gating_output, "gating_output"), (topk_weight, "topk_weight"),
+                 (topk_indices, "topk_indices"), (token_expert_indices, "token_expert_indices")):
+        _need_contig(t, n)
+    if num_tokens == 0:
+        return
+    with torch.cuda.device(gating_output.device):
+        lib().topk_softmax(_ptr(gating_output), _ptr(topk_weight), _ptr(topk_indices),
+                           _ptr(token_expert_indices), num_experts, num_tokens, top_k,
+                           _stream(gating_output.device))
+        st = lib().moe_last_status()
+    if st != MOE_OK:
+        raise MoeError(st, "topk_softmax")
+
+
+def topk_softmax(gating_output: torch.Tensor, top_k: int, renormalize: bool = False):
+    """Allocating router: returns (weights [T,k] f32, indices [T,k] int32,
+    token_expert_indices [T,k] int32).  renormalize divides the k weights by their sum."""
+    _need_cuda(gating_output, "gating_output")
+    _need_contig(gating_output, "gating_output")
+    if gating_output.dtype != torch.float32 or gating_output.dim() != 2:
+        raise TypeError("gating_output must be a rank-2 float32 tensor")
+    T, E = gating_output.shape
+    dev = gating_output.device
+    w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    src = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_topk_softmax_v2(_ptr(gating_output), _ptr(w), _ptr(idx), _ptr(src), E, T,
+                                       top_k, int(renormalize), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_topk_softmax_v2")
+    return w, idx, src
+
+
+# ---------------------------------------------------------------------------------------------
+# sort / align: kernels/preprocessing.cuh:253-313
+# ---------------------------------------------------------------------------------------------
+
+def route_prep(expert_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int):
+    """Returns (expert_offsets [E+2] int32, sorted_token_ids [T*k] int32, sorted_weights [T*k]
+    f32).  Entries past expert_offsets[E] are left unwritten."""
+    _need_cuda(expert_indices, "expert_indices")
+    _need_contig(expert_indices, "expert_indices")
+    _need_contig(routing_weights, "routing_weights")
+    T, k = expert_indices.shape
+    dev = expert_indices.device
+    offsets = torch.empty((num_experts + 2,), dtype=torch.int32, device=dev)
+    st_ids = torch.empty((max(T * k, 1),), dtype=torch.int32, device=dev)
+    st_w = torch.empty((max(T * k, 1),), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_route_prep(_ptr(expert_indices), _ptr(routing_weights), T, k, num_experts,
+                                  _ptr(offsets), _ptr(st_ids), _ptr(st_w), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_route_prep")
+    return offsets, st_ids[:T * k], st_w[:T * k]
+
+
+# ---------------------------------------------------------------------------------------------
+# fused MoE: src/lib.rs:157-335
+# ---------------------------------------------------------------------------------------------
+
+class Activation(enum.IntEnum):
+    """src/lib.rs:157-172 (to_int: Silu=0, Gelu=1, Relu=2)."""
+    Silu = 0
+    Gelu = 1
+    Relu = 2
+
+    def to_int(self) -> int:
+        return int(self)
+
+
+def fused_moe_internal_dtype(dtype: torch.dtype) -> int:
+    """src/lib.rs:174-182."""
+    if dtype == torch.float16:
+        return 0
+    if dtype == torch.bfloat16:
+        return 1
+    if dtype == torch.float32:
+        return 2
+    raise TypeError(f"dtype {dtype} is not supported")
+
+
+def validate_moe_inputs(input, gate_weights, up_weights, down_weights, routing_weights,
+                        expert_indices, num_experts, num_selected_experts, moe_type):
+    """src/lib.rs:185-242, same checks and messages; returns (num_tokens, hidden_dim)."""
+    if input.dim() != 2:
+        raise ValueError(f"input must be rank 2, got {tuple(input.shape)}")
+    num_tokens, hidden_dim = input.shape
+    if gate_weights.dim() != 3 or up_weights.dim() != 3:
+        raise ValueError("gate_weights and up_weights must be rank 3")
+    ne_g, hd_g, id_g = gate_weights.shape
+    ne_u, hd_u, id_u = up_weights.shape
+    if down_weights is not None:
+        if down_weights.dim() != 3:
+            raise ValueError("down_weights must be rank 3")
+        ne_d, id_d, hd_d = down_weights.shape
+    else:
+        ne_d, id_d, hd_d = num_experts, id_u, hd_u
+    if routing_weights.dim() != 2 or expert_indices.dim() != 2:
+        raise ValueError("routing_weights and expert_indices must be rank 2")
+    nt, nse = routing_weights.shape
+    nt2, nse2 = expert_indices.shape
+    if ne_g != num_experts or ne_u != num_experts or ne_d != num_experts:
+        raise ValueError("Number of experts mismatch")
+    if hd_g != hidden_dim or hd_u != hidden_dim:
+        raise ValueError("Hidden dimension mismatch for gate/up weights")
+    if hd_d != hidden_dim:
+        raise ValueError(f"Hidden dimension mismatch for down weights (expected {hidden_dim}, "
+                         f"got {hd_d})")
+    if id_g != id_u or id_u != id_d:
+        raise ValueError(f"Intermediate dimension mismatch (gate: {id_g}, up: {id_u}, "
+                         f"down: {id_d})")
+    if nt != num_tokens or nt2 != num_tokens:
+        raise ValueError("Number of tokens mismatch")
+    if nse != num_selected_experts or nse2 != num_selected_experts:
+        raise ValueError("Number of selected experts mismatch")
+    if moe_type > 1:
+        raise ValueError("moe_type must be one of 0 or 1")
+    return num_tokens, hidden_dim
+
+
+def workspace_size(num_tokens: int, hidden_dim: int, intermediate_dim: int, num_experts: int,
+                   top_k: int, moe_type: int, dtype: torch.dtype) -> int:
+    return int(lib().moe_fused_workspace_size(num_tokens, hidden_dim, intermediate_dim,
+                                              num_experts, top_k, moe_type,
+                                              fused_moe_internal_dtype(dtype)))
+
+
+def fused_moe(input, gate_weights, up_weights, down_weights, routing_weights, expert_indices,
+              num_experts: int, top_k: int, activation: int, moe_type: int,
+              out: Optional[torch.Tensor] = None,
+              workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Status-checked fused MoE (moe_fused_v2).  Tensors must already be validated; `out` is
+    allocated when not given; `workspace` (uint8, >= workspace_size() bytes) is optional."""
+    T, H = input.shape
+    I = gate_weights.shape[2]
+    dev = input.device
+    if out is None:
+        out = torch.empty((T, H), dtype=input.dtype, device=dev)
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = _ptr(workspace), workspace.numel() * workspace.element_size()
+    with torch.cuda.device(dev):
+        st = lib().moe_fused_v2(_ptr(input), _ptr(gate_weights), _ptr(up_weights),
+                                _ptr(down_weights), _ptr(routing_weights), _ptr(expert_indices),
+                                _ptr(out), T, H, I, num_experts, top_k, int(activation),
+                                moe_type, fused_moe_internal_dtype(input.dtype), ws_ptr, ws_bytes,
+                                _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_fused_v2")
+    return out
+
+
+class FusedMoE:
+    """src/lib.rs:244-335."""
+
+    def __init__(self, num_experts: int, num_selected_experts: int,
+                 activation: Activation = Activation.Silu):
+        self.num_experts = num_experts
+        self.num_selected_experts = num_selected_experts
+        self.activation = Activation(activation)
+
+    @classmethod
+    def new(cls, num_experts: int, num_selected_experts: int, activation: Activation):
+        return cls(num_experts, num_selected_experts, activation)
+
+    def forward(self, input: torch.Tensor, gate_weights: torch.Tensor, up_weights: torch.Tensor,
+                down_weights: Optional[torch.Tensor], routing_weights: torch.Tensor,
+                expert_indices: torch.Tensor, moe_type: int) -> torch.Tensor:
+        """input [T,H]; gate/up [E,H,I]; down [E,I,H] (Qwen3, moe_type 0) or None (Nomic,
+        moe_type 1); routing_weights [T,k] f32; expert_indices [T,k] int32/uint32.  Returns
+        [T,H] in input's dtype."""
+        validate_moe_inputs(input, gate_weights, up_weights, down_weights, routing_weights,
+                            expert_indices, self.num_experts, self.num_selected_experts, moe_type)
+        dt = input.dtype
+        fused_moe_internal_dtype(dt)
+        tensors = [("input", input), ("gate_weights", gate_weights), ("up_weights", up_weights),
+                   ("routing_weights", routing_weights), ("expert_indices", expert_indices)]
+        if down_weights is not None:
+            tensors.append(("down_weights", down_weights))
+        for n, t in tensors:
+            _need_cuda(t, n)
+            _need_contig(t, n)
+        for n, t in (("gate_weights", gate_weights), ("up_weights", up_weights),
+                     ("down_weights", down_weights)):
+            if t is not None and t.dtype != dt:
+                raise TypeError(f"{n} must have the input's dtype {dt}, got {t.dtype}")
+        if routing_weights.dtype != torch.float32:
+            raise TypeError("routing_weights must be float32")
+        if expert_indices.dtype not in _INDEX_DTYPES:
+            raise TypeError("expert_indices must be int32 or uint32")
+        if moe_type == 0 and down_weights is None:
+            raise ValueError("moe_type 0 (Qwen3) needs down_weights")
+        return fused_moe(input, gate_weights, up_weights, down_weights, routing_weights,
+                         expert_indices, self.num_experts, self.num_selected_experts,
+                         self.activation.to_int(), moe_type)
+
+
+def device_error_bits(device: int = 0, clear: bool = False) -> int:
+    return int(lib().moe_device_error_bits(device, int(clear)))
+
+
+def set_gemm_path(path: int) -> int:
+    """0 automatic, 1 SIMT only, 2 tensor cores only; returns the previous setting."""
+    return int(lib().moe_set_gemm_path(path))
+
+
+def last_gemm_path() -> int:
+    return int(lib().moe_last_gemm_path())

@@ -1,0 +1,434 @@
+// C ABI of candle-moe-b200 (declared in include/candle_moe.h): argument checks, per-device
+// state, the stream-ordered workspace pool, TMA tensor maps and the dispatch of the router,
+// route-preparation, grouped-GEMM and combine kernels.
+//
+// Reference counterparts: topk_softmax -> kernels/topk_softmax.cu:331-353; fused_moe ->
+// kernels/moe.cu:451-773 (direct/GEMM path selection, per-call workspace, preprocessing,
+// per-dtype dispatch); moe_route_prep -> kernels/preprocessing.cuh:253-313.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <climits>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/candle_moe.h"
+#include "common.cuh"
+#include "kernels.h"
+
+#define CMOE_API extern "C" __attribute__((visibility("default")))
+
+namespace cmoe {
+namespace {
+
+thread_local int t_last_status = MOE_OK;
+thread_local int t_last_path = 0;
+std::atomic<int> g_gemm_path{0};
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::atomic<bool> ready{false};
+  int num_sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  cudaMemPool_t pool = nullptr;
+  uint32_t* err_word = nullptr;
+};
+
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int init_device(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return MOE_ERR_UNSUPPORTED;
+  DeviceState& d = g_dev[dev];
+  if (d.ready.load(std::memory_order_acquire)) {
+    *out = &d;
+    return MOE_OK;
+  }
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!d.ready.load(std::memory_order_relaxed)) {
+    if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return MOE_ERR_CUDA;
+    cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaMemPoolProps props;
+    std::memset(&props, 0, sizeof(props));
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    if (cudaMemPoolCreate(&d.pool, &props) != cudaSuccess) return MOE_ERR_CUDA;
+    uint64_t keep = UINT64_MAX;  // keep freed blocks cached for the next call
+    cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (cudaMalloc(&d.err_word, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
+    if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
+    route_prep_set_attributes();
+    sm100_set_attributes();
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+              cudaSuccess &&
+          q == cudaDriverEntryPointSuccess)
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    d.ready.store(true, std::memory_order_release);
+  }
+  *out = &d;
+  return MOE_OK;
+}
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+  return init_device(dev, out);
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// 2-D tensor map over a row-major [outer, inner] matrix of 16-bit elements, 128-byte swizzle.
+bool make_map_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint32_t box_inner, uint32_t box_outer) {
+  if (!g_encode) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Workspace of one fused call (byte offsets into one buffer).
+struct FusedLayout {
+  size_t offsets, tile_prefix, sorted_token, sorted_flat, sorted_w, prep_scratch, inter, slot,
+      total;
+};
+
+FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype) {
+  const int64_t rows = T * k;
+  const size_t elt = dtype == kF32 ? 4 : 2;
+  FusedLayout L;
+  size_t o = 0;
+  L.offsets = o;        o += align256(sizeof(int32_t) * (E + 2));
+  L.tile_prefix = o;    o += align256(sizeof(int32_t) * (E + 1));
+  L.sorted_token = o;   o += align256(sizeof(int32_t) * rows);
+  L.sorted_flat = o;    o += align256(sizeof(int32_t) * rows);
+  L.sorted_w = o;       o += align256(sizeof(float) * rows);
+  L.prep_scratch = o;   o += align256(route_prep_scratch_bytes(rows, E));
+  L.inter = o;          o += align256(elt * static_cast<size_t>(rows) * I);
+  L.slot = o;           o += (k > 1) ? align256(elt * static_cast<size_t>(rows) * H) : 0;
+  L.total = o;
+  return L;
+}
+
+int finish(int status) {
+  if (status == MOE_OK) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) status = MOE_ERR_CUDA;
+  }
+  return status;
+}
+
+bool sm100_shape_ok(int dtype, const void* x, const void* g, const void* u, const void* d,
+                    const void* out, int H, int I, int moe_type) {
+  if (dtype == kF32) return false;
+  if (H % 128 != 0 || I % 128 != 0) return false;
+  if (!aligned16(x) || !aligned16(g) || !aligned16(u) || !aligned16(out)) return false;
+  if (moe_type == 0 && !aligned16(d)) return false;
+  return true;
+}
+
+int fused_impl(const void* input, const void* gate, const void* up, const void* down,
+               const float* rw, const uint32_t* idx, void* output, int64_t T, int H, int I, int E,
+               int k, int act, uint32_t moe_type, uint32_t dtype, void* workspace,
+               size_t workspace_bytes, cudaStream_t stream) {
+  t_last_path = 0;
+  if (dtype > 2 || moe_type > 1) return MOE_ERR_INVALID_ARG;
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return MOE_ERR_INVALID_ARG;
+  if (T == 0) return MOE_OK;
+  if (!input || !gate || !up || !rw || !idx || !output) return MOE_ERR_INVALID_ARG;
+  if (moe_type == 0 && !down) return MOE_ERR_INVALID_ARG;
+  if (E > route_prep_max_experts()) return MOE_ERR_UNSUPPORTED;
+  if (T * k > INT32_MAX) return MOE_ERR_UNSUPPORTED;
+
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+
+  const int gpath = g_gemm_path.load();
+  bool use_sm100 = sm100_shape_ok(static_cast<int>(dtype), input, gate, up, down, output, H, I,
+                                  static_cast<int>(moe_type)) &&
+                   ds->cc_major == 10 && g_encode != nullptr;
+  if (gpath == 1) use_sm100 = false;
+  if (gpath == 2 && !use_sm100) return MOE_ERR_UNSUPPORTED;
+  const int bm = use_sm100 ? sm100_tile_m() : simt_tile_m();
+
+  const FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype));
+  char* ws = static_cast<char*>(workspace);
+  bool owned = false;
+  if (ws == nullptr) {
+    void* p = nullptr;
+    if (cudaMallocFromPoolAsync(&p, L.total, ds->pool, stream) != cudaSuccess) {
+      cudaGetLastError();
+      return MOE_ERR_NO_MEMORY;
+    }
+    ws = static_cast<char*>(p);
+    owned = true;
+  } else if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
+    return MOE_ERR_WORKSPACE;
+  }
+
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* tile_prefix = reinterpret_cast<int32_t*>(ws + L.tile_prefix);
+  int32_t* s_token = reinterpret_cast<int32_t*>(ws + L.sorted_token);
+  int32_t* s_flat = reinterpret_cast<int32_t*>(ws + L.sorted_flat);
+  float* s_w = reinterpret_cast<float*>(ws + L.sorted_w);
+  void* prep_scratch = ws + L.prep_scratch;
+  void* inter = ws + L.inter;
+  void* slot = (k > 1) ? static_cast<void*>(ws + L.slot) : output;
+
+  const int64_t rows = T * k;
+  const int64_t mtile_bound = rows / bm + (E < rows ? E : rows);
+  const size_t elt = dtype == kF32 ? 4 : 2;
+
+  st = launch_route_prep(idx, rw, T, k, E, bm, offsets, tile_prefix, s_token, s_w, s_flat,
+                         prep_scratch, stream) == 0
+           ? MOE_OK
+           : MOE_ERR_UNSUPPORTED;
+  if (st == MOE_OK && k == 1)
+    if (cudaMemsetAsync(output, 0, elt * static_cast<size_t>(T) * H, stream) != cudaSuccess)
+      st = MOE_ERR_CUDA;
+
+  if (st == MOE_OK && use_sm100) {
+    // GEMM-1
+    CUtensorMap mA, mB0, mB1;
+    const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
+    const int bn1 = (mode1 == kModeG1Single && I % 256 == 0) ? 256 : 128;
+    const int cols1 = sm100_out_cols(mode1, bn1);
+    bool ok = make_map_2d(&mA, dtype, input, H, T, 64, 1) &&
+              make_map_2d(&mB0, dtype, gate, I, static_cast<uint64_t>(E) * H, 64, 64) &&
+              make_map_2d(&mB1, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 64);
+    Sm100Params p;
+    p.offsets = offsets;
+    p.tile_prefix = tile_prefix;
+    p.sorted_token = s_token;
+    p.sorted_flat = s_flat;
+    p.sorted_w = s_w;
+    p.E = E;
+    p.act = act;
+    p.err = ds->err_word;
+    if (ok) {
+      p.out = inter;
+      p.N = I;
+      p.K = H;
+      p.n_tiles = I / cols1;
+      const int64_t tiles = mtile_bound * p.n_tiles;
+      const int grid = static_cast<int>(tiles < ds->num_sms ? tiles : ds->num_sms);
+      if (launch_sm100_gemm(static_cast<int>(dtype), mode1, bn1, mA, mB0, mB1, p, grid, stream))
+        ok = false;
+    }
+    // GEMM-2
+    const int mode2 = moe_type == 0 ? kModeG2MN : kModeG2K;
+    const int bn2 = H % 256 == 0 ? 256 : 128;
+    if (ok) {
+      ok = make_map_2d(&mA, dtype, inter, I, static_cast<uint64_t>(rows), 64, 128);
+      if (mode2 == kModeG2MN)
+        ok = ok && make_map_2d(&mB0, dtype, down, H, static_cast<uint64_t>(E) * I, 64, 64);
+      else
+        ok = ok && make_map_2d(&mB0, dtype, up, I, static_cast<uint64_t>(E) * H, 64, bn2);
+    }
+    if (ok) {
+      p.out = slot;
+      p.N = H;
+      p.K = I;
+      p.n_tiles = H / sm100_out_cols(mode2, bn2);
+      const int64_t tiles = mtile_bound * p.n_tiles;
+      const int grid = static_cast<int>(tiles < ds->num_sms ? tiles : ds->num_sms);
+      if (launch_sm100_gemm(static_cast<int>(dtype), mode2, bn2, mA, mB0, mB0, p, grid, stream))
+        ok = false;
+    }
+    if (!ok) st = MOE_ERR_CUDA;
+    t_last_path = 2;
+  } else if (st == MOE_OK) {
+    SimtParams p;
+    p.offsets = offsets;
+    p.tile_prefix = tile_prefix;
+    p.sorted_token = s_token;
+    p.sorted_flat = s_flat;
+    p.sorted_w = s_w;
+    p.E = E;
+    p.act = act;
+    p.a = input;
+    p.b0 = gate;
+    p.b1 = up;
+    p.out = inter;
+    p.N = I;
+    p.K = H;
+    st = launch_simt_gemm(static_cast<int>(dtype), moe_type == 0 ? 0 : 1, p, mtile_bound, stream) == 0
+             ? MOE_OK
+             : MOE_ERR_UNSUPPORTED;
+    if (st == MOE_OK) {
+      p.a = inter;
+      p.b0 = moe_type == 0 ? down : up;
+      p.b1 = nullptr;
+      p.out = slot;
+      p.N = H;
+      p.K = I;
+      st = launch_simt_gemm(static_cast<int>(dtype), moe_type == 0 ? 2 : 3, p, mtile_bound, stream) == 0
+               ? MOE_OK
+               : MOE_ERR_UNSUPPORTED;
+    }
+    t_last_path = 1;
+  }
+  if (st == MOE_OK && k > 1)
+    launch_combine(static_cast<int>(dtype), slot, idx, T, k, H, E, output, ds->num_sms, stream);
+  if (owned) cudaFreeAsync(ws, stream);
+  return finish(st);
+}
+
+}  // namespace
+}  // namespace cmoe
+
+using namespace cmoe;
+
+CMOE_API int moe_last_status(void) { return t_last_status; }
+
+CMOE_API const char* moe_status_string(int status) {
+  switch (status) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_INVALID_ARG: return "invalid argument";
+    case MOE_ERR_UNSUPPORTED: return "unsupported";
+    case MOE_ERR_CUDA: return "cuda error";
+    case MOE_ERR_WORKSPACE: return "workspace too small or misaligned";
+    case MOE_ERR_NO_MEMORY: return "out of device memory";
+    default: return "unknown status";
+  }
+}
+
+CMOE_API int moe_topk_softmax_v2(const float* gating_output, float* topk_weights,
+                                 int32_t* topk_indices, int32_t* token_expert_indices,
+                                 int32_t num_experts, int64_t num_tokens, int32_t topk,
+                                 int32_t renormalize, void* stream) {
+  if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MOE_OK;
+  if (num_tokens > INT32_MAX) return MOE_ERR_UNSUPPORTED;
+  if (!gating_output || !topk_weights || !topk_indices || !token_expert_indices)
+    return MOE_ERR_INVALID_ARG;
+  if ((num_experts & (num_experts - 1)) != 0 || num_experts > 256) return MOE_ERR_UNSUPPORTED;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_router(gating_output, topk_weights, topk_indices, token_expert_indices, num_experts,
+                    static_cast<int>(num_tokens), topk, renormalize, ds->num_sms,
+                    static_cast<cudaStream_t>(stream)) != 0)
+    return MOE_ERR_UNSUPPORTED;
+  return finish(MOE_OK);
+}
+
+CMOE_API void topk_softmax(void* gating_output, void* topk_weights, void* topk_indices,
+                           void* token_expert_indices, int32_t num_experts, int32_t num_tokens,
+                           int32_t topk, void* stream) {
+  t_last_status = moe_topk_softmax_v2(
+      static_cast<const float*>(gating_output), static_cast<float*>(topk_weights),
+      static_cast<int32_t*>(topk_indices), static_cast<int32_t*>(token_expert_indices),
+      num_experts, num_tokens, topk, 0, stream);
+}
+
+CMOE_API int moe_route_prep(const uint32_t* expert_indices, const float* routing_weights,
+                            int64_t num_tokens, int32_t topk, int32_t num_experts,
+                            int32_t* expert_offsets, int32_t* sorted_token_ids,
+                            float* sorted_weights, void* stream) {
+  if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
+  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
+    return MOE_ERR_UNSUPPORTED;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t scratch_bytes = route_prep_scratch_bytes(num_tokens * topk, num_experts);
+  void* scratch = nullptr;
+  if (scratch_bytes) {
+    if (cudaMallocFromPoolAsync(&scratch, scratch_bytes, ds->pool, s) != cudaSuccess) {
+      cudaGetLastError();
+      return MOE_ERR_NO_MEMORY;
+    }
+  }
+  st = launch_route_prep(expert_indices, routing_weights, num_tokens, topk, num_experts, 1,
+                         expert_offsets, nullptr, sorted_token_ids, sorted_weights, nullptr,
+                         scratch, s) == 0
+           ? MOE_OK
+           : MOE_ERR_UNSUPPORTED;
+  if (scratch) cudaFreeAsync(scratch, s);
+  return finish(st);
+}
+
+CMOE_API size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim,
+                                         int32_t intermediate_dim, int32_t num_experts,
+                                         int32_t topk, uint32_t moe_type, uint32_t dtype) {
+  (void)moe_type;
+  if (num_tokens <= 0 || hidden_dim <= 0 || intermediate_dim <= 0 || num_experts <= 0 ||
+      topk <= 0 || dtype > 2)
+    return 0;
+  return fused_layout(num_tokens, hidden_dim, intermediate_dim, num_experts, topk,
+                      static_cast<int>(dtype))
+      .total;
+}
+
+CMOE_API int moe_fused_v2(const void* input, const void* gate_weights, const void* up_weights,
+                          const void* down_weights, const float* routing_weights,
+                          const uint32_t* expert_indices, void* output, int64_t num_tokens,
+                          int32_t hidden_dim, int32_t intermediate_dim, int32_t num_experts,
+                          int32_t topk, int32_t activation_type, uint32_t moe_type,
+                          uint32_t dtype, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  return fused_impl(input, gate_weights, up_weights, down_weights, routing_weights,
+                    expert_indices, output, num_tokens, hidden_dim, intermediate_dim,
+                    num_experts, topk, activation_type, moe_type, dtype, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+CMOE_API void fused_moe(void* input, void* gate_weights, void* up_weights, void* down_weights,
+                        void* routing_weights, void* expert_indices, void* output,
+                        int num_tokens, int hidden_dim, int intermediate_dim, int num_experts,
+                        int num_selected_experts, int activation_type, uint32_t moe_type,
+                        uint32_t dtype, void* stream) {
+  t_last_status = fused_impl(input, gate_weights, up_weights, down_weights,
+                             static_cast<const float*>(routing_weights),
+                             static_cast<const uint32_t*>(expert_indices), output, num_tokens,
+                             hidden_dim, intermediate_dim, num_experts, num_selected_experts,
+                             activation_type, moe_type, dtype, nullptr, 0,
+                             static_cast<cudaStream_t>(stream));
+}
+
+CMOE_API uint32_t moe_device_error_bits(int32_t device, int32_t clear) {
+  DeviceState* ds = nullptr;
+  if (init_device(device, &ds) != MOE_OK) return 0xffffffffu;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  uint32_t v = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpy(&v, ds->err_word, sizeof(v), cudaMemcpyDeviceToHost);
+  if (clear) cudaMemset(ds->err_word, 0, sizeof(uint32_t));
+  cudaSetDevice(prev);
+  return v;
+}
+
+CMOE_API int32_t moe_set_gemm_path(int32_t path) {
+  if (path < 0 || path > 2) return -1;
+  return g_gemm_path.exchange(path);
+}
+
+CMOE_API int32_t moe_last_gemm_path(void) { return t_last_path; }

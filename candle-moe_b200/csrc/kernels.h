@@ -1,0 +1,74 @@
+// Internal interface between the C-ABI layer (capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace cmoe {
+
+// ---- router.cu -------------------------------------------------------------------------------
+int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int num_experts,
+                  int num_tokens, int k, int renorm, int num_sms, cudaStream_t stream);
+
+// ---- route_prep.cu ---------------------------------------------------------------------------
+size_t route_prep_scratch_bytes(int64_t rows, int E);
+int route_prep_max_experts();
+void route_prep_set_attributes();
+int launch_route_prep(const uint32_t* idx, const float* wts, int64_t num_tokens, int k, int E,
+                      int bm, int32_t* offsets, int32_t* tile_prefix, int32_t* s_token,
+                      float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream);
+
+// ---- moe_simt.cu -----------------------------------------------------------------------------
+struct SimtParams {
+  const void* a;                // GEMM-1: x [T, K]; GEMM-2: intermediate [rows, K]
+  const void* b0;               // GEMM-1: gate [E, K, N]; GEMM-2: down [E, K, N] or up [E, N, K]
+  const void* b1;               // GEMM-1 Qwen3: up [E, K, N]
+  const int32_t* offsets;       // [E+2]
+  const int32_t* tile_prefix;   // [E+1], tile height simt_tile_m()
+  const int32_t* sorted_token;  // [rows]
+  const int32_t* sorted_flat;   // [rows]
+  const float* sorted_w;        // [rows]
+  void* out;                    // GEMM-1: intermediate [rows, N]; GEMM-2: slot [T*k, N] / out [T, N]
+  int N, K, E, act;
+};
+int simt_tile_m();
+int launch_simt_gemm(int dtype, int mode, const SimtParams& p, int64_t mtile_bound,
+                     cudaStream_t s);
+int launch_combine(int dtype, const void* slot, const uint32_t* idx, int64_t num_tokens, int k,
+                   int H, int E, void* out, int num_sms, cudaStream_t s);
+
+// ---- moe_sm100.cu ----------------------------------------------------------------------------
+// GEMM modes shared by both grouped-GEMM families
+enum GemmMode : int {
+  kModeG1Dual = 0,    // Qwen3 GEMM-1: act(x.G) * (x.U)
+  kModeG1Single = 1,  // Nomic GEMM-1: act(x.G)
+  kModeG2MN = 2,      // Qwen3 GEMM-2: h.D (D_e [I,H], N contiguous) * w
+  kModeG2K = 3,       // Nomic GEMM-2: h.U^T (U_e [H,I], K contiguous) * w
+};
+
+struct Sm100Params {
+  const int32_t* offsets;       // [E+2]
+  const int32_t* tile_prefix;   // [E+1], tile height sm100_tile_m()
+  const int32_t* sorted_token;  // [rows]
+  const int32_t* sorted_flat;   // [rows]
+  const float* sorted_w;        // [rows]
+  void* out;                    // GEMM-1: intermediate [rows, N]; GEMM-2: slot [T*k, N] / out [T, N]
+  int N;                        // output columns (I for GEMM-1, H for GEMM-2)
+  int K;                        // reduction length (H for GEMM-1, I for GEMM-2)
+  int E;
+  int act;
+  int n_tiles;                  // N / output columns per tile
+  uint32_t* err;                // device error word
+};
+int sm100_tile_m();
+int sm100_tile_k();
+size_t sm100_smem_bytes();
+void sm100_set_attributes();
+// Output columns covered by one tile of `mode` with B tile width bn (128 or 256).
+int sm100_out_cols(int mode, int bn);
+int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
+                      const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
+
+}  // namespace cmoe

@@ -1,0 +1,237 @@
+// SIMT grouped GEMMs and the slot combine.
+//
+// The f32 MoE (kernels/moe.cu:193-449 in the reference) and any f16/bf16 shape the tcgen05 path
+// does not take (hidden / intermediate sizes that are not multiples of its tile sizes, or
+// misaligned pointers) run here: 64x64 output tiles, 16-deep K slices staged through shared
+// memory as f32, 4x4 outputs per thread, f32 accumulation.  The grid's y dimension enumerates
+// the linear m-tiles of all experts (tile_prefix from route preparation, tile height 64), so no
+// CTA is launched for rows an expert does not have.
+//
+// Modes (one template instance each):
+//   0  Qwen3 GEMM-1: h = act(A.G_e) * (A.U_e), A = gathered x rows   (moe.cu:193-317, has_up)
+//   1  Nomic GEMM-1: h = act(A.G_e)                                    (moe.cu:193-317)
+//   2  Qwen3 GEMM-2: y = h.D_e (D_e [I,H], N contiguous) times the routing weight
+//   3  Nomic GEMM-2: y = h.U_e^T (U_e [H,I], K contiguous) times the routing weight
+//                                                                      (moe.cu:319-449)
+// GEMM-1 writes the intermediate row of each sorted row in the operand type (the reference's
+// f16/bf16 path rounds it there too, nomic_moe.cu:374, qwen3_moe.cu:493).  GEMM-2 writes each
+// weighted contribution to its (token, slot) row of a slot buffer; combine_slots then sums the
+// k slots of a token in slot order in f32 and rounds once.  With k = 1 GEMM-2 writes the output
+// row directly.
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cmoe {
+
+constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16, kSimtThreads = 256;
+
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm_kernel(SimtParams p) {
+  __shared__ __align__(16) float As[kSimtBK][kSimtBM + 4];
+  __shared__ __align__(16) float Bs[kSimtBK][kSimtBN + 4];
+  __shared__ __align__(16) float Bs2[MODE == 0 ? kSimtBK : 1][kSimtBN + 4];
+  __shared__ int64_t s_arow[kSimtBM];
+
+  const int mt = blockIdx.y;
+  const int E = p.E, N = p.N, K = p.K;
+  if (mt >= __ldg(p.tile_prefix + E)) return;
+  const int e = expert_of_tile(p.tile_prefix, E, mt);
+  const int m0 = (mt - __ldg(p.tile_prefix + e)) * kSimtBM;
+  const int row_base = __ldg(p.offsets + e) + m0;
+  const int cnt = __ldg(p.offsets + e + 1) - __ldg(p.offsets + e);
+  const int valid = min(kSimtBM, cnt - m0);
+  const int n0 = blockIdx.x * kSimtBN;
+  const int tid = threadIdx.x;
+  if (tid < kSimtBM) {
+    const int r = min(tid, valid - 1);
+    s_arow[tid] = (MODE <= 1) ? static_cast<int64_t>(__ldg(p.sorted_token + row_base + r))
+                              : static_cast<int64_t>(row_base + r);
+  }
+  __syncthreads();
+
+  const T* A = static_cast<const T*>(p.a);
+  const size_t wstride = static_cast<size_t>(K) * N;
+  const T* B0 = static_cast<const T*>(p.b0) + static_cast<size_t>(e) * wstride;
+  const T* B1 = (MODE == 0) ? static_cast<const T*>(p.b1) + static_cast<size_t>(e) * wstride : nullptr;
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][4], acc2[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = acc2[i][j] = 0.f;
+
+  for (int k0 = 0; k0 < K; k0 += kSimtBK) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int li = tid + q * kSimtThreads;
+      const int r = li >> 4, c = li & 15;
+      const int kk = k0 + c;
+      As[c][r] = kk < K ? Elem<T>::to_f(A[s_arow[r] * K + kk]) : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int li = tid + q * kSimtThreads;
+      if (MODE == 3) {
+        // B[kk][n] = U[n][kk]: walk K fastest for coalescing
+        const int n = li >> 4, c = li & 15;
+        const int kk = k0 + c, nn = n0 + n;
+        Bs[c][n] = (kk < K && nn < N) ? Elem<T>::to_f(B0[static_cast<size_t>(nn) * K + kk]) : 0.f;
+      } else {
+        const int c = li >> 6, n = li & 63;
+        const int kk = k0 + c, nn = n0 + n;
+        const bool ok = kk < K && nn < N;
+        Bs[c][n] = ok ? Elem<T>::to_f(B0[static_cast<size_t>(kk) * N + nn]) : 0.f;
+        if (MODE == 0) Bs2[c][n] = ok ? Elem<T>::to_f(B1[static_cast<size_t>(kk) * N + nn]) : 0.f;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kSimtBK; ++kk) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+      if (MODE == 0) {
+        const float4 u4 = *reinterpret_cast<const float4*>(&Bs2[kk][tx * 4]);
+        const float u[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc2[i][j] = fmaf(a[i], u[j], acc2[i][j]);
+      }
+    }
+    __syncthreads();
+  }
+
+  T* out = static_cast<T*>(p.out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = ty * 4 + i;
+    if (r >= valid) continue;
+    int64_t orow;
+    float wgt = 1.f;
+    if (MODE <= 1) {
+      orow = row_base + r;
+    } else {
+      orow = __ldg(p.sorted_flat + row_base + r);
+      wgt = __ldg(p.sorted_w + row_base + r);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      float v;
+      if (MODE == 0) v = act_apply(acc[i][j], p.act) * acc2[i][j];
+      else if (MODE == 1) v = act_apply(acc[i][j], p.act);
+      else v = acc[i][j] * wgt;
+      out[orow * N + n] = Elem<T>::from_f(v);
+    }
+  }
+}
+
+// out[t, :] = sum over slots j < k whose expert id is < E of slot[t*k + j, :], in slot order,
+// accumulated in f32 and rounded once.  V elements (16 bytes) per thread when H allows it.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) combine_slots_kernel(const T* __restrict__ slot,
+                                                            const uint32_t* __restrict__ idx,
+                                                            int64_t num_tokens, int k, int H,
+                                                            int E, T* __restrict__ out) {
+  const int vec_per_row = H / V;
+  const int64_t total = num_tokens * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = v / vec_per_row;
+    const int c = static_cast<int>(v - t * vec_per_row) * V;
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      if (__ldg(idx + t * k + j) >= static_cast<uint32_t>(E)) continue;
+      const T* src = slot + (t * k + j) * H + c;
+      if (V * sizeof(T) == 16) {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
+        const T* qe = reinterpret_cast<const T*>(&q);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(src[i]);
+      }
+    }
+    T* dst = out + t * H + c;
+    if (V * sizeof(T) == 16) {
+      uint4 q;
+      T* qe = reinterpret_cast<T*>(&q);
+#pragma unroll
+      for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
+      *reinterpret_cast<uint4*>(dst) = q;
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) dst[i] = Elem<T>::from_f(acc[i]);
+    }
+  }
+}
+
+// ---- host launchers --------------------------------------------------------------------------
+
+template <typename T>
+static void simt_launch_t(int mode, const SimtParams& p, int64_t mtile_bound, cudaStream_t s) {
+  dim3 grid((p.N + kSimtBN - 1) / kSimtBN, static_cast<unsigned>(mtile_bound));
+  switch (mode) {
+    case 0: simt_grouped_gemm_kernel<T, 0><<<grid, kSimtThreads, 0, s>>>(p); break;
+    case 1: simt_grouped_gemm_kernel<T, 1><<<grid, kSimtThreads, 0, s>>>(p); break;
+    case 2: simt_grouped_gemm_kernel<T, 2><<<grid, kSimtThreads, 0, s>>>(p); break;
+    default: simt_grouped_gemm_kernel<T, 3><<<grid, kSimtThreads, 0, s>>>(p); break;
+  }
+}
+
+int simt_tile_m() { return kSimtBM; }
+
+// mtile_bound: an upper bound of the number of linear m-tiles (grid y); CTAs past the real
+// count exit at once.
+int launch_simt_gemm(int dtype, int mode, const SimtParams& p, int64_t mtile_bound,
+                     cudaStream_t s) {
+  if (mtile_bound <= 0) return 0;
+  if (mtile_bound > 65535) return 2;
+  if (dtype == kF32) simt_launch_t<float>(mode, p, mtile_bound, s);
+  else if (dtype == kBF16) simt_launch_t<__nv_bfloat16>(mode, p, mtile_bound, s);
+  else simt_launch_t<__half>(mode, p, mtile_bound, s);
+  return 0;
+}
+
+template <typename T>
+static void combine_t(const void* slot, const uint32_t* idx, int64_t T_, int k, int H, int E,
+                      void* out, int num_sms, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = (H % V) == 0 && (reinterpret_cast<uintptr_t>(slot) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+  const int64_t work = T_ * (vec ? H / V : H);
+  int64_t blocks = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (vec)
+    combine_slots_kernel<T, V><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+  else
+    combine_slots_kernel<T, 1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+}
+
+int launch_combine(int dtype, const void* slot, const uint32_t* idx, int64_t num_tokens, int k,
+                   int H, int E, void* out, int num_sms, cudaStream_t s) {
+  if (num_tokens <= 0) return 0;
+  if (dtype == kF32) combine_t<float>(slot, idx, num_tokens, k, H, E, out, num_sms, s);
+  else if (dtype == kBF16) combine_t<__nv_bfloat16>(slot, idx, num_tokens, k, H, E, out, num_sms, s);
+  else combine_t<__half>(slot, idx, num_tokens, k, H, E, out, num_sms, s);
+  return 0;
+}
+
+}  // namespace cmoe

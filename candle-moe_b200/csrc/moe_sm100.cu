@@ -1,0 +1,370 @@
+// G1/G2: persistent grouped GEMMs of the f16/bf16 expert FFN on the 5th-generation tensor cores.
+//
+// Replaces the reference's wmma grouped GEMMs (nomic_moe.cu:259-807 / 1114-1662 and
+// qwen3_moe.cu:354-966 / 1289-1903) for hidden / intermediate sizes that are multiples of the
+// tile sizes.  One CTA per SM walks the linear tile list (m-tile of an expert x n-tile), with
+// warp roles:
+//   warp 0     TMA producer.  GEMM-1 gathers the 128 token rows of an m-tile straight from x
+//              with tile::gather4 (four rows per copy, one copy per lane); GEMM-2 reads the
+//              contiguous intermediate rows with one tiled copy.  B tiles come from the expert's
+//              weights in their API layout: gate/up [E,H,I] and down [E,I,H] as MN-major
+//              operands, Nomic's up [E,H,I] as the K-major operand of h.U^T.
+//   warp 1     one thread issues tcgen05.mma (M=128, N=128/256, K=16, f32 accumulate in TMEM)
+//              and tcgen05.commit to release smem stages and publish accumulators.
+//   warp 2     allocates / frees the 512 TMEM columns (two accumulator buffers of 256).
+//   warps 4-7  epilogue: tcgen05.ld the accumulator (one TMEM lane per output row), apply the
+//              fused epilogue and store 64-byte row segments:
+//                GEMM-1 Qwen3  act(g)*u  -> intermediate row (operand type)
+//                GEMM-1 Nomic  act(g)    -> intermediate row
+//                GEMM-2        acc*w     -> (token, slot) row of the slot buffer, or the output
+//                                           row itself when k = 1
+// Operands are staged with 128-byte swizzle in a 4-stage mbarrier ring (48 KB per stage).
+// Every wait is bounded (common.cuh); a timeout sets a bit in the device error word.
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cmoe {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kAStageBytes = kBM * kBK * 2;                      // 16 KB
+constexpr int kBStageBytesMax = 256 * kBK * 2;                   // 32 KB
+constexpr int kStageBytes = kAStageBytes + kBStageBytesMax;      // 48 KB
+constexpr int kTmemCols = 512;
+constexpr int kAccStride = 256;                                  // TMEM columns per buffer
+constexpr int kSm100Threads = 256;
+constexpr size_t kSm100Smem = static_cast<size_t>(kStages) * kStageBytes + 1024;
+
+template <int MODE, int BN>
+struct TileCfg {
+  static constexpr int kMmaN = (MODE == kModeG1Dual) ? 128 : BN;
+  static constexpr int kOutCols = (MODE == kModeG1Dual) ? 128 : BN;
+  static constexpr int kBBytes = (MODE == kModeG1Dual) ? 2 * 128 * kBK * 2 : BN * kBK * 2;
+  static constexpr uint32_t kTxBytes = kAStageBytes + kBBytes;
+};
+
+template <typename T> struct UmmaFmt;
+template <> struct UmmaFmt<__half> { static constexpr uint32_t v = 0; };
+template <> struct UmmaFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
+
+struct TileInfo {
+  int e, row_base, valid, n0;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const Sm100Params& p, int tile, int out_cols) {
+  TileInfo ti;
+  const int mt = tile / p.n_tiles;
+  const int nt = tile - mt * p.n_tiles;
+  ti.e = expert_of_tile(p.tile_prefix, p.E, mt);
+  const int m0 = (mt - __ldg(p.tile_prefix + ti.e)) * kBM;
+  const int off = __ldg(p.offsets + ti.e);
+  ti.row_base = off + m0;
+  ti.valid = min(kBM, __ldg(p.offsets + ti.e + 1) - off - m0);
+  ti.n0 = nt * out_cols;
+  return ti;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack2<T>(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack2<T>(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack2<T>(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack2<T>(v[q * 8 + 6], v[q * 8 + 7]);
+    d[q] = w;
+  }
+}
+
+template <typename T, int MODE, int BN>
+__global__ void __launch_bounds__(kSm100Threads, 1)
+    sm100_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                              const __grid_constant__ CUtensorMap tmB0,
+                              const __grid_constant__ CUtensorMap tmB1, const Sm100Params p) {
+  using C = TileCfg<MODE, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[kStages];
+  __shared__ __align__(8) uint64_t bar_empty[kStages];
+  __shared__ __align__(8) uint64_t bar_accf[2];
+  __shared__ __align__(8) uint64_t bar_acce[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t smem_base = (raw + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_tiles = __ldg(p.tile_prefix + p.E) * p.n_tiles;
+  const int num_kb = p.K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_addr(&bar_full[s]), 1);
+      mbar_init(smem_addr(&bar_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&bar_accf[b]), 1);
+      mbar_init(smem_addr(&bar_acce[b]), 4);
+    }
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    if (MODE == kModeG1Dual) tma_prefetch_desc(&tmB1);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_addr(&s_tmem), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      const TileInfo ti = decode_tile(p, tile, C::kOutCols);
+      int tok0 = 0, tok1 = 0, tok2 = 0, tok3 = 0;
+      if (MODE == kModeG1Dual || MODE == kModeG1Single) {
+        const int r = lane * 4;
+        const int last = ti.valid - 1;
+        tok0 = __ldg(p.sorted_token + ti.row_base + min(r + 0, last));
+        tok1 = __ldg(p.sorted_token + ti.row_base + min(r + 1, last));
+        tok2 = __ldg(p.sorted_token + ti.row_base + min(r + 2, last));
+        tok3 = __ldg(p.sorted_token + ti.row_base + min(r + 3, last));
+      }
+      for (int kb = 0; kb < num_kb; ++kb) {
+        bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
+                                     kErrWaitEmpty);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = smem_addr(&bar_full[stage]);
+        if (lane == 0) mbar_arrive_expect_tx(full, C::kTxBytes);
+        __syncwarp();
+        const uint32_t a_dst = smem_base + stage * kStageBytes;
+        const uint32_t b_dst = a_dst + kAStageBytes;
+        const int kc = kb * kBK;
+        if (MODE == kModeG1Dual || MODE == kModeG1Single) {
+          tma_gather4(a_dst + lane * 4 * 128, &tmA, full, kc, tok0, tok1, tok2, tok3);
+        } else if (lane == 0) {
+          tma_load_2d(a_dst, &tmA, full, kc, ti.row_base);
+        }
+        if (lane == 0) {
+          if (MODE == kModeG1Dual) {
+            const int krow = ti.e * p.K + kc;
+            tma_load_2d(b_dst, &tmB0, full, ti.n0, krow);
+            tma_load_2d(b_dst + 8192, &tmB0, full, ti.n0 + 64, krow);
+            tma_load_2d(b_dst + 16384, &tmB1, full, ti.n0, krow);
+            tma_load_2d(b_dst + 24576, &tmB1, full, ti.n0 + 64, krow);
+          } else if (MODE == kModeG1Single || MODE == kModeG2MN) {
+            const int krow = ti.e * p.K + kc;
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB0, full, ti.n0 + j * 64, krow);
+          } else {
+            tma_load_2d(b_dst, &tmB0, full, kc, ti.e * p.N + ti.n0);
+          }
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc =
+          umma_idesc(UmmaFmt<T>::v, MODE == kModeG2K ? 0u : 1u, kBM, C::kMmaN);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int lt = 0;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        const uint32_t par = static_cast<uint32_t>((lt >> 1) & 1) ^ 1u;
+        if (!mbar_wait_bounded(smem_addr(&bar_acce[buf]), par, &s_abort, p.err, kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kAccStride);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_addr(&bar_full[stage]), phase, &s_abort, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_base + stage * kStageBytes;
+          const uint32_t b_base = a_base + kAStageBytes;
+#pragma unroll
+          for (int ks = 0; ks < kBK / 16; ++ks) {
+            const uint64_t adesc = umma_sdesc(a_base + ks * 32, 16, 1024);
+            const uint32_t acc = (kb | ks) != 0 ? 1u : 0u;
+            if (MODE == kModeG1Dual) {
+              umma_f16(d, adesc, umma_sdesc(b_base + ks * 2048, 8192, 1024), idesc, acc);
+              umma_f16(d + 128, adesc, umma_sdesc(b_base + 16384 + ks * 2048, 8192, 1024), idesc, acc);
+            } else if (MODE == kModeG2K) {
+              umma_f16(d, adesc, umma_sdesc(b_base + ks * 32, 16, 1024), idesc, acc);
+            } else {
+              umma_f16(d, adesc, umma_sdesc(b_base + ks * 2048, 8192, 1024), idesc, acc);
+            }
+          }
+          umma_commit(smem_addr(&bar_empty[stage]));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_addr(&bar_accf[buf]));
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp - 4;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    T* out = static_cast<T*>(p.out);
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++lt) {
+      const TileInfo ti = decode_tile(p, tile, C::kOutCols);
+      const int buf = lt & 1;
+      bool got = mbar_wait_bounded(smem_addr(&bar_accf[buf]), static_cast<uint32_t>((lt >> 1) & 1),
+                                   &s_abort, p.err, kErrWaitAccFull);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                          static_cast<uint32_t>(buf * kAccStride);
+      const bool live = r < ti.valid;
+      int64_t orow = 0;
+      float wgt = 1.f;
+      if (MODE == kModeG1Dual || MODE == kModeG1Single) {
+        orow = ti.row_base + r;
+      } else if (live) {
+        orow = __ldg(p.sorted_flat + ti.row_base + r);
+        wgt = __ldg(p.sorted_w + ti.row_base + r);
+      }
+      T* dst_row = out + orow * p.N + ti.n0;
+      if (MODE == kModeG1Dual) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(tb + c, g);
+          tmem_ld_32x32b_x32(tb + 128 + c, u);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(g[i]), p.act) * __uint_as_float(u[i]);
+          if (live) store_row32<T>(dst_row + c, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t a[32];
+          tmem_ld_32x32b_x32(tb + c, a);
+          tmem_ld_wait();
+          float v[32];
+          if (MODE == kModeG1Single) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(a[i]), p.act);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) * wgt;
+          }
+          if (live) store_row32<T>(dst_row + c, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&bar_acce[buf]));
+    }
+  }
+
+  __syncthreads();
+  if (s_abort) {
+    // a role gave up: leave time for copies and MMAs already in flight before releasing TMEM
+    const unsigned long long t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---- host side -------------------------------------------------------------------------------
+
+int sm100_tile_m() { return kBM; }
+int sm100_tile_k() { return kBK; }
+size_t sm100_smem_bytes() { return kSm100Smem; }
+
+int sm100_out_cols(int mode, int bn) { return mode == kModeG1Dual ? 128 : bn; }
+
+template <typename T, int MODE, int BN>
+static void set_attr_one() {
+  cudaFuncSetAttribute(sm100_grouped_gemm_kernel<T, MODE, BN>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSm100Smem));
+}
+
+template <typename T>
+static void set_attr_t() {
+  set_attr_one<T, kModeG1Dual, 128>();
+  set_attr_one<T, kModeG1Single, 128>();
+  set_attr_one<T, kModeG1Single, 256>();
+  set_attr_one<T, kModeG2MN, 128>();
+  set_attr_one<T, kModeG2MN, 256>();
+  set_attr_one<T, kModeG2K, 128>();
+  set_attr_one<T, kModeG2K, 256>();
+}
+
+void sm100_set_attributes() {
+  set_attr_t<__nv_bfloat16>();
+  set_attr_t<__half>();
+}
+
+template <typename T>
+static int launch_t(int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
+                    const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s) {
+#define CMOE_SM100(MODE, BN)                                                                 \
+  sm100_grouped_gemm_kernel<T, MODE, BN><<<grid, kSm100Threads, kSm100Smem, s>>>(a, b0, b1, p); \
+  return 0;
+  switch (mode) {
+    case kModeG1Dual:
+      CMOE_SM100(kModeG1Dual, 128)
+    case kModeG1Single:
+      if (bn == 256) { CMOE_SM100(kModeG1Single, 256) }
+      CMOE_SM100(kModeG1Single, 128)
+    case kModeG2MN:
+      if (bn == 256) { CMOE_SM100(kModeG2MN, 256) }
+      CMOE_SM100(kModeG2MN, 128)
+    case kModeG2K:
+      if (bn == 256) { CMOE_SM100(kModeG2K, 256) }
+      CMOE_SM100(kModeG2K, 128)
+    default:
+      return 1;
+  }
+#undef CMOE_SM100
+}
+
+int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
+                      const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s) {
+  if (grid <= 0) return 0;
+  if (dtype == kBF16) return launch_t<__nv_bfloat16>(mode, bn, a, b0, b1, p, grid, s);
+  if (dtype == kF16) return launch_t<__half>(mode, bn, a, b0, b1, p, grid, s);
+  return 1;
+}
+
+}  // namespace cmoe

@@ -1,0 +1,160 @@
+// R1: fused softmax + top-k router (replaces kernels/topk_softmax.cu:136-353).
+//
+// One row (token) is owned by a group of TPR lanes; each lane loads its VPT logits with 128-bit
+// loads, the group reduces max / sum with xor shuffles, then runs k rounds of a shuffle argmax
+// (ties go to the lower expert, topk_softmax.cu:240) and clears the winner to -10000
+// (topk_softmax.cu:256-264).  The lane grouping and the order in which a lane sums its values
+// are those of the reference launcher (topk_softmax.cu:268-295), and this file is compiled with
+// --use_fast_math like the reference build (build.rs:59), so the weights come out bit-identical
+// to the reference kernel's.  Differences from the reference: a grid-stride loop sized to the
+// SM count instead of one CTA per 4 warps of rows, an optional renormalisation of the k weights
+// (Qwen3 norm_topk_prob), and a status return for unsupported expert counts.
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cmoe {
+
+template <int E>
+struct RouterGeom {
+  static constexpr int kBytes = (4 * E < 16) ? 4 * E : 16;
+  static constexpr int kElts = kBytes / 4;  // floats per vector load
+  static constexpr int kVecs = (E / (kElts * 32)) > 1 ? (E / (kElts * 32)) : 1;
+  static constexpr int kVpt = kVecs * kElts;  // values per lane
+  static constexpr int kTpr = E / kVpt;       // lanes per row
+  static constexpr int kRpw = 32 / kTpr;      // rows per warp
+};
+
+template <int N> struct alignas(4 * N) FVec { float v[N]; };
+
+template <int E>
+__global__ void __launch_bounds__(256) router_topk_softmax_kernel(
+    const float* __restrict__ logits, float* __restrict__ out_w, int32_t* __restrict__ out_idx,
+    int32_t* __restrict__ out_src, int num_tokens, int k, int renorm) {
+  using G = RouterGeom<E>;
+  constexpr int kElts = G::kElts, kVpt = G::kVpt, kTpr = G::kTpr, kVecs = G::kVecs;
+  const int lane = threadIdx.x & 31;
+  const int g = lane % kTpr;    // position of this lane in its row group
+  const int sub = lane / kTpr;  // row of the group within the warp
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t warp0 = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * warps_per_block;
+
+  for (int64_t wbase = warp0 * G::kRpw; wbase < num_tokens; wbase += warp_stride * G::kRpw) {
+    const int64_t row = wbase + sub;
+    const bool active = row < num_tokens;
+    float v[kVpt];
+    if (active) {
+      const float* rp = logits + row * E + g * kElts;
+#pragma unroll
+      for (int l = 0; l < kVecs; ++l) {
+        const FVec<kElts> q = *reinterpret_cast<const FVec<kElts>*>(rp + l * kElts * kTpr);
+#pragma unroll
+        for (int i = 0; i < kElts; ++i) v[l * kElts + i] = q.v[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVpt; ++i) v[i] = 0.f;
+    }
+    // softmax (max subtracted), same operation order as the reference
+    float m = v[0];
+#pragma unroll
+    for (int i = 1; i < kVpt; ++i) m = max(m, v[i]);
+#pragma unroll
+    for (int mask = kTpr / 2; mask > 0; mask /= 2) m = max(m, __shfl_xor_sync(0xffffffffu, m, mask, kTpr));
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kVpt; ++i) {
+      v[i] = expf(v[i] - m);
+      s += v[i];
+    }
+#pragma unroll
+    for (int mask = kTpr / 2; mask > 0; mask /= 2) s += __shfl_xor_sync(0xffffffffu, s, mask, kTpr);
+    const float rs = 1.f / s;
+#pragma unroll
+    for (int i = 0; i < kVpt; ++i) v[i] = v[i] * rs;
+
+    // k rounds of group argmax
+    const int col0 = g * kElts;
+    float wsum = 0.f;
+    for (int j = 0; j < k; ++j) {
+      float best = v[0];
+      int be = col0;
+#pragma unroll
+      for (int l = 0; l < kVecs; ++l) {
+#pragma unroll
+        for (int i = 0; i < kElts; ++i) {
+          const float x = v[l * kElts + i];
+          if (x > best) {
+            best = x;
+            be = col0 + l * kElts * kTpr + i;
+          }
+        }
+      }
+#pragma unroll
+      for (int mask = kTpr / 2; mask > 0; mask /= 2) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, mask, kTpr);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, mask, kTpr);
+        if (ob > best || (ob == best && oe < be)) {
+          best = ob;
+          be = oe;
+        }
+      }
+      wsum += best;
+      if (active && g == 0) {
+        const int64_t o = row * k + j;
+        out_w[o] = best;
+        out_idx[o] = be;
+        out_src[o] = static_cast<int32_t>(static_cast<int64_t>(j) * num_tokens + row);
+      }
+      // the owning lane clears the winner
+      if (g == (be / kElts) % kTpr) {
+        const int l = be / (kElts * kTpr);
+        const int i = be % kElts;
+#pragma unroll
+        for (int ll = 0; ll < kVecs; ++ll)
+#pragma unroll
+          for (int ii = 0; ii < kElts; ++ii)
+            if (ll == l && ii == i) v[ll * kElts + ii] = -10000.f;
+      }
+    }
+    if (renorm && active && g == 0) {
+      for (int j = 0; j < k; ++j) out_w[row * k + j] = out_w[row * k + j] / wsum;
+    }
+  }
+}
+
+// Returns 0 on success, 1 for an unsupported expert count.
+int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int num_experts,
+                  int num_tokens, int k, int renorm, int num_sms, cudaStream_t stream) {
+  if (num_tokens <= 0) return 0;
+  const int threads = 256;
+  auto grid_for = [&](int rows_per_warp) {
+    const int64_t warps = (static_cast<int64_t>(num_tokens) + rows_per_warp - 1) / rows_per_warp;
+    int64_t blocks = (warps + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+    return static_cast<int>(blocks < cap ? blocks : cap);
+  };
+#define CMOE_ROUTER_CASE(EE)                                                                    \
+  case EE:                                                                                    \
+    router_topk_softmax_kernel<EE><<<grid_for(RouterGeom<EE>::kRpw), threads, 0, stream>>>(   \
+        logits, w, idx, src, num_tokens, k, renorm);                                          \
+    return 0;
+  switch (num_experts) {
+    CMOE_ROUTER_CASE(1)
+    CMOE_ROUTER_CASE(2)
+    CMOE_ROUTER_CASE(4)
+    CMOE_ROUTER_CASE(8)
+    CMOE_ROUTER_CASE(16)
+    CMOE_ROUTER_CASE(32)
+    CMOE_ROUTER_CASE(64)
+    CMOE_ROUTER_CASE(128)
+    CMOE_ROUTER_CASE(256)
+    default:
+      return 1;
+  }
+#undef CMOE_ROUTER_CASE
+}
+
+}  // namespace cmoe

@@ -1,0 +1,144 @@
+/*
+ * candle-moe-b200: C ABI of the Blackwell (sm_100a) fused-MoE library.
+ *
+ * The first two entry points are drop-in replacements for the two symbols that the reference
+ * crate kozistr/candle-moe declares in src/ffi.rs and links from its static libmoe.a; its Rust
+ * layer (src/lib.rs) can call them unchanged.  The remaining entry points extend the interface
+ * with status returns, caller-owned workspace and the sort/align step on its own.
+ *
+ * Conventions (all entry points):
+ *   - every pointer is a CUDA device pointer to contiguous row-major data; the caller owns all
+ *     buffers;
+ *   - work is enqueued on `stream` (a cudaStream_t / CUstream; NULL = the legacy default
+ *     stream) and the call returns without synchronising;
+ *   - dtype codes: 0 = f16, 1 = bf16, 2 = f32; activation codes: 0 = SiLU, 1 = GELU (tanh form),
+ *     2 = ReLU (any other value = SiLU); moe_type: 0 = Qwen3 (gate/up/down), 1 = Nomic
+ *     (fc1 -> act -> fc2, the second matrix applied transposed).
+ */
+#ifndef CANDLE_MOE_B200_H
+#define CANDLE_MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes of the extended entry points (and of moe_last_status()). */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG 1   /* bad size, code or null pointer */
+#define MOE_ERR_UNSUPPORTED 2   /* valid request outside what the library implements */
+#define MOE_ERR_CUDA 3          /* a CUDA call or kernel launch failed */
+#define MOE_ERR_WORKSPACE 4     /* caller workspace smaller than moe_fused_workspace_size() */
+#define MOE_ERR_NO_MEMORY 5     /* the library's workspace pool could not allocate */
+
+/*
+ * Fused softmax + top-k router.  Replaces kernels/topk_softmax.cu:331-353 (declared for Rust at
+ * src/ffi.rs:15-24).
+ *   gating_output        [num_tokens, num_experts] f32 router logits
+ *   topk_weights         [num_tokens, topk] f32 out: softmax probability of each pick (not
+ *                        renormalised, as in the reference)
+ *   topk_indices         [num_tokens, topk] i32/u32 out: expert id of each pick, descending
+ *                        probability, ties to the lower id
+ *   token_expert_indices [num_tokens, topk] i32/u32 out: j*num_tokens + t
+ *   num_experts          power of two, 1..256
+ * num_tokens is int32_t here: the reference C definition says int64_t but its Rust caller passes
+ * a c_int (src/ffi.rs:21 vs topk_softmax.cu:337); this declaration matches the caller.
+ * Errors (unsupported num_experts, launch failure) are reported by moe_last_status().
+ */
+void topk_softmax(void* gating_output, void* topk_weights, void* topk_indices,
+                  void* token_expert_indices, int32_t num_experts, int32_t num_tokens,
+                  int32_t topk, void* stream);
+
+/*
+ * Fused MoE expert FFN.  Replaces kernels/moe.cu:451-773 (declared for Rust at
+ * src/ffi.rs:45-62).
+ *   input            [num_tokens, hidden_dim]                       dtype
+ *   gate_weights     [num_experts, hidden_dim, intermediate_dim]     dtype
+ *   up_weights       [num_experts, hidden_dim, intermediate_dim]     dtype
+ *   down_weights     [num_experts, intermediate_dim, hidden_dim]     dtype (Qwen3), NULL (Nomic)
+ *   routing_weights  [num_tokens, num_selected_experts]              f32
+ *   expert_indices   [num_tokens, num_selected_experts]              u32 (ids >= num_experts are
+ *                                                                    skipped)
+ *   output           [num_tokens, hidden_dim]                        dtype, out
+ * Qwen3: out[t] = sum_j w[t,j] * (act(x_t.G_e) * (x_t.U_e)).D_e ;  Nomic: out[t] = sum_j w[t,j] *
+ * act(x_t.G_e).U_e^T, with e = expert_indices[t,j].  The reference required a zeroed output and
+ * accumulated into it; this library overwrites it, which gives the same result for every input
+ * the reference accepts.  Workspace comes from a library-owned stream-ordered pool.  Errors are
+ * reported by moe_last_status().
+ */
+void fused_moe(void* input, void* gate_weights, void* up_weights, void* down_weights,
+               void* routing_weights, void* expert_indices, void* output, int num_tokens,
+               int hidden_dim, int intermediate_dim, int num_experts, int num_selected_experts,
+               int activation_type, uint32_t moe_type, uint32_t dtype, void* stream);
+
+/* Status of the last drop-in call (topk_softmax / fused_moe) made by this thread. */
+int moe_last_status(void);
+
+/* Human-readable name of a status code. */
+const char* moe_status_string(int status);
+
+/*
+ * Router with a status return and optional renormalisation of the k weights (w / sum_j w, as
+ * Qwen3's norm_topk_prob does; the reference has no such option).  Same semantics as
+ * topk_softmax (kernels/topk_softmax.cu:331-353) otherwise.
+ */
+int moe_topk_softmax_v2(const float* gating_output, float* topk_weights, int32_t* topk_indices,
+                        int32_t* token_expert_indices, int32_t num_experts, int64_t num_tokens,
+                        int32_t topk, int32_t renormalize, void* stream);
+
+/*
+ * Sort / align step on its own.  Replaces launch_preprocessing (kernels/preprocessing.cuh:253-313),
+ * which the reference runs inside fused_moe without exporting it.
+ *   expert_offsets    [num_experts + 2] i32 out: exclusive prefix of per-expert row counts,
+ *                     [num_experts] = routed rows, [num_experts + 1] = largest count
+ *   sorted_token_ids  [num_tokens * topk] i32 out: token id of each routed row, grouped by expert
+ *   sorted_weights    [num_tokens * topk] f32 out: routing weight of each routed row
+ * Within an expert, rows are in ascending (token, slot) order (the reference's order there
+ * depends on atomics).  Scratch memory, when needed, comes from the library's pool.
+ */
+int moe_route_prep(const uint32_t* expert_indices, const float* routing_weights,
+                   int64_t num_tokens, int32_t topk, int32_t num_experts, int32_t* expert_offsets,
+                   int32_t* sorted_token_ids, float* sorted_weights, void* stream);
+
+/* Bytes of caller workspace that moe_fused_v2 needs for these sizes (0 for num_tokens == 0). */
+size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim, int32_t intermediate_dim,
+                                int32_t num_experts, int32_t topk, uint32_t moe_type,
+                                uint32_t dtype);
+
+/*
+ * fused_moe with a status return and optional caller-owned workspace (workspace == NULL: use the
+ * library pool; else it must hold moe_fused_workspace_size() bytes, 256-byte aligned, and must
+ * not be in use by another call still running on the GPU).  Same semantics as fused_moe
+ * (kernels/moe.cu:451-773) otherwise.
+ */
+int moe_fused_v2(const void* input, const void* gate_weights, const void* up_weights,
+                 const void* down_weights, const float* routing_weights,
+                 const uint32_t* expert_indices, void* output, int64_t num_tokens,
+                 int32_t hidden_dim, int32_t intermediate_dim, int32_t num_experts, int32_t topk,
+                 int32_t activation_type, uint32_t moe_type, uint32_t dtype, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
+ * Error bits the tensor-core kernels raised on `device` (a bounded wait that ran out; see
+ * DevErr in csrc/common.cuh).  Synchronises the device.  clear != 0 resets them.
+ */
+uint32_t moe_device_error_bits(int32_t device, int32_t clear);
+
+/*
+ * Kernel family selection for the f16/bf16 expert GEMMs: 0 = automatic (tensor cores where the
+ * shape allows), 1 = always the SIMT kernels, 2 = tensor cores only (unsupported shapes then
+ * return MOE_ERR_UNSUPPORTED).  Process-wide; returns the previous value.
+ */
+int32_t moe_set_gemm_path(int32_t path);
+
+/* Which family served the last moe_fused_v2 / fused_moe call of this thread: 1 SIMT, 2 tensor
+ * cores, 0 none. */
+int32_t moe_last_gemm_path(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CANDLE_MOE_B200_H */
