@@ -1,0 +1,402 @@
+"""Benchmark of the candle-moe-b200 hot path (router + fused MoE expert FFN).
+
+Default workload (N=1): BASELINE config 5, the Qwen3-30B-A3B-shaped MoE layer -- bf16, 65536
+tokens, hidden 2048, moe_intermediate 768, 128 experts, top-8, SwiGLU, renormalised top-k
+weights, router logits N(0,1) + a per-expert N(0,0.5) bias.  One step = topk_softmax on the
+[65536,128] logits + FusedMoE.forward (route preparation, two tcgen05 grouped GEMMs, combine).
+Inputs are seeded synthetic tensors (no datasets exist for this layer); weights ~N(0,0.02),
+hidden ~N(0,1).  The weights (1.2 GB) and activations (256 MB) are larger than the 126 MB L2,
+so no explicit flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1..c5]
+
+N>1 (torchrun, one rank per GPU): each rank runs its own replica of the workload (the
+expert-parallel exchange is not in this version), value = tokens of all ranks / max-over-ranks
+time.  --impl reference times the reference's algorithm on the host cores (the CPU oracle port,
+all threads) on a bounded token sample per step; the reference crate has no CPU implementation
+of its own and its CUDA GEMM kernels cannot launch at these sizes.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "candle-moe_b200")]
+
+CONFIGS = {
+    # name: (dtype, moe_type, act, T, H, I, E, k, renormalize, bias_std)
+    "c1": ("f32", None, None, 512, None, None, 8, 2, False, 0.0),         # router only
+    "c2": ("f32", 1, 1, 512, 768, 3072, 8, 2, False, 0.0),
+    "c3": ("bf16", 1, 1, 32768, 768, 3072, 8, 2, False, 0.0),
+    "c4": ("bf16", 0, 0, 32768, 4096, 1536, 8, 2, True, 0.0),
+    "c4-f16": ("f16", 0, 0, 32768, 4096, 1536, 8, 2, True, 0.0),
+    "c5": ("bf16", 0, 0, 65536, 2048, 768, 128, 8, True, 0.5),
+}
+WORKLOAD_NAMES = {
+    "c1": "topk-softmax router, 512 tokens x 8 experts, top-2 (BASELINE config 1)",
+    "c2": "Nomic MoE f32, 512 tokens, H768 I3072, 8 experts top-2, GELU (BASELINE config 2)",
+    "c3": "Nomic MoE bf16, 32768 tokens, H768 I3072, 8 experts top-2, GELU (BASELINE config 3)",
+    "c4": "Qwen3 MoE bf16, 32768 tokens, H4096 I1536, 8 experts top-2, SwiGLU (BASELINE config 4)",
+    "c4-f16": "Qwen3 MoE f16, 32768 tokens, H4096 I1536, 8 experts top-2 (BASELINE config 4)",
+    "c5": "Qwen3-30B-A3B-shaped MoE layer bf16, 65536 tokens, H2048 I768, 128 experts top-8, "
+          "SwiGLU, biased router (BASELINE config 5)",
+}
+METRIC = "fused-MoE tokens/s"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic(kernel_key):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(kernel_key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                sm.append(float(row[1]))
+                mx = float(row[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, row[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        loaded = [s for s in sm if mx and s > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, value):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(cfg, seed=0):
+    """Seeded synthetic inputs on the current GPU."""
+    import torch
+    dtype, moe_type, act, T, H, I, E, k, renorm, bias_std = cfg
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    logits = torch.randn(T, E, generator=g, device="cuda")
+    if bias_std:
+        logits += torch.randn(E, generator=g, device="cuda") * bias_std
+    inp = {"logits": logits}
+    if moe_type is None:
+        return inp
+    inp["x"] = torch.randn(T, H, generator=g, device="cuda").to(tdt)
+    inp["gate"] = (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(tdt)
+    inp["up"] = (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(tdt)
+    inp["down"] = ((torch.randn(E, I, H, generator=g, device="cuda") * 0.02).to(tdt)
+                   if moe_type == 0 else None)
+    return inp
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    import candle_moe
+
+    cfg = CONFIGS[args.config]
+    dtype, moe_type, act, T, H, I, E, k, renorm, _ = cfg
+    inp = make_inputs(cfg, seed=0)
+    router_only = moe_type is None
+    moe = None if router_only else candle_moe.FusedMoE(E, k, candle_moe.Activation(act))
+    stream = torch.cuda.current_stream()
+
+    def step(logits, x):
+        w, idx, _ = candle_moe.topk_softmax(logits, k, renormalize=renorm)
+        if router_only:
+            return w
+        return moe.forward(x, inp["gate"], inp["up"], inp["down"], w, idx, moe_type)
+
+    x_dev = None if router_only else inp["x"]
+    for _ in range(args.warmup):
+        step(inp["logits"], x_dev)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region -------------------------------------------------------
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = candle_moe.kernel_launches()
+    candle_moe.phase_timing(True)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(inp["logits"], x_dev)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    candle_moe.phase_timing(False)
+    clk = clocks.stop()
+    ms_total = ev0.elapsed_time(ev1)
+    launches = candle_moe.kernel_launches() - launches0
+    phases, ncalls = (candle_moe.phase_times() if not router_only else ({}, 0))
+    ms_step = max_over_ranks(world, ms_total / args.steps)
+    value = T * world / (ms_step / 1e3)
+
+    # ---- end to end through the public API: host inputs in, host output out ------------------
+    h_logits = inp["logits"].cpu().pin_memory()
+    h_x = None if router_only else inp["x"].cpu().pin_memory()
+    out_shape = (T, k) if router_only else (T, H)
+    out_dtype = torch.float32 if router_only else inp["x"].dtype
+    h_out = torch.empty(out_shape, dtype=out_dtype).pin_memory()
+    h2d = h_logits.numel() * 4 + (0 if router_only else h_x.numel() * h_x.element_size())
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        lg = h_logits.to("cuda", non_blocking=True)
+        xx = None if router_only else h_x.to("cuda", non_blocking=True)
+        out = step(lg, xx)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(min(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
+
+    peaks, peak_kind = load_peaks()
+    line = {
+        "metric": METRIC if not router_only else "topk-softmax us",
+        "value": value if not router_only else ms_step * 1e3,
+        "unit": "tokens/s" if not router_only else "us",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": not router_only, "scaling": "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic (seeded torch.randn; weights N(0,0.02), hidden N(0,1))",
+        "config": {"workload": WORKLOAD_NAMES[args.config], "tokens": T, "hidden": H,
+                   "intermediate": I, "experts": E, "top_k": k,
+                   "parallelism": "replicas" if world > 1 else "single-gpu",
+                   "l2": "inputs larger than L2 (weights 1.2 GB + activations), no flush"
+                   if args.config == "c5" else "no flush"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if router_only:
+        line["value"] = ms_step * 1e3
+    if not router_only and ncalls:
+        rows = T * k
+        n_up = 2 if moe_type == 0 else 1
+        flops = {"gemm1": 2.0 * rows * H * I * n_up, "gemm2": 2.0 * rows * I * H}
+        per_call = {p: phases[p] / ncalls for p in phases}
+        dom = max(("gemm1", "gemm2"), key=lambda p: per_call[p])
+        achieved = flops[dom] / (per_call[dom] / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        line["roofline"] = {
+            "kernel": f"sm100_grouped_gemm ({dom})", "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": f"{peak_kind} bf16 dense, sustained (kernel timed inside a long step)",
+            "traffic": load_traffic(f"{args.config}:{dom}"),
+            "flops_per_launch": flops[dom],
+        }
+        line["phases_ms"] = per_call
+        line["tflops_total"] = (flops["gemm1"] + flops["gemm2"]) / (ms_step / 1e3) / 1e12
+    line["e2e"] = {"value": T * world / (e2e_ms / 1e3) if not router_only else e2e_ms * 1e3,
+                   "unit": line["unit"], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                   "ms_per_step": e2e_ms}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not router_only:
+        line["cpu_baseline"] = cpu_baseline(cfg, inp, target_s=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(cfg, inp, target_s=10.0):
+    """The reference algorithm (CPU oracle port, all host threads) on a token sample."""
+    import numpy as np
+    import oracle
+    dtype, moe_type, act, T, H, I, E, k, renorm, _ = cfg
+
+    def raw(t):
+        import torch
+        t = t.contiguous().cpu()
+        if t.dtype == torch.float32:
+            return t.numpy()
+        return t.view(torch.int16).numpy().view(np.uint16)
+
+    G, U = raw(inp["gate"]), raw(inp["up"])
+    D = raw(inp["down"]) if inp["down"] is not None else None
+    logits = inp["logits"].cpu().numpy()
+    x_all = raw(inp["x"])
+
+    def run(n):
+        w, idx, _, _ = oracle.topk_softmax(logits[:n], k, renormalize=renorm)
+        t0 = time.perf_counter()
+        oracle.moe_forward(x_all[:n], G, U, D, w, idx, activation=act, moe_type=moe_type,
+                           dtype=dtype)
+        return time.perf_counter() - t0
+
+    n = min(T, 256)
+    dt = run(n)
+    n2 = int(min(T, max(n, n * target_s / max(dt, 1e-3))))
+    dt = run(n2)
+    return {"value": n2 / dt, "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"first {n2} tokens of the workload, {dt:.1f} s",
+            "seconds": dt}
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's algorithm on the host cores (CPU oracle port)."""
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    cfg = CONFIGS[args.config]
+    dtype, moe_type, act, T, H, I, E, k, renorm, bias_std = cfg
+    # the same seeded distributions as our arm, generated on the host
+    logits = oracle.randn(11, (T, E))
+    if bias_std:
+        logits = np.ascontiguousarray(logits + oracle.randn(12, (E,), std=bias_std)[None, :])
+    if moe_type is None:
+        sample = T
+        run = lambda: oracle.topk_softmax(logits, k, renormalize=renorm)  # noqa: E731
+    else:
+        x = oracle.randn(13, (T, H), dtype=dtype)
+        G = oracle.randn(14, (E, H, I), std=0.02, dtype=dtype)
+        U = oracle.randn(15, (E, H, I), std=0.02, dtype=dtype)
+        D = oracle.randn(16, (E, I, H), std=0.02, dtype=dtype) if moe_type == 0 else None
+        sample = min(T, args.ref_sample)
+
+        def run():
+            w, idx, _, _ = oracle.topk_softmax(logits[:sample], k, renormalize=renorm)
+            oracle.moe_forward(x[:sample], G, U, D, w, idx, activation=act, moe_type=moe_type,
+                               dtype=dtype)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / args.steps
+    router_only = moe_type is None
+    value = dt * 1e6 if router_only else sample / dt
+    unit = "us" if router_only else "tokens/s"
+    line = {
+        "impl": "reference", "metric": METRIC if not router_only else "topk-softmax us",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": not router_only,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD_NAMES[args.config], "tokens": T, "hidden": H,
+                   "intermediate": I, "experts": E, "top_k": k},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": oracle.num_threads(),
+                         "kind": "port",
+                         "sample": f"{sample} of {T} tokens per step (router + naive "
+                                   "per-expert loop, f32 accumulate, OpenMP)"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference crate has no CPU implementation; this is its algorithm restated "
+                "in C (oracle/) on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c5")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-sample", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="override the token count (small profiling cases)")
+    args = ap.parse_args()
+    if args.tokens:
+        CONFIGS[args.config] = CONFIGS[args.config][:3] + (args.tokens,) + CONFIGS[args.config][4:]
+        WORKLOAD_NAMES[args.config] += f" [tokens overridden: {args.tokens}]"
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -72,6 +72,12 @@ def lib() -> ctypes.CDLL:
         L.moe_set_gemm_path.restype = I32
         L.moe_last_gemm_path.argtypes = []
         L.moe_last_gemm_path.restype = I32
+        L.moe_kernel_launches.argtypes = []
+        L.moe_kernel_launches.restype = I64
+        L.moe_phase_timing.argtypes = [I32]
+        L.moe_phase_timing.restype = ctypes.c_int
+        L.moe_phase_times.argtypes = [P, P]
+        L.moe_phase_times.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -351,3 +357,26 @@ def set_gemm_path(path: int) -> int:
 
 def last_gemm_path() -> int:
     return int(lib().moe_last_gemm_path())
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(lib().moe_kernel_launches())
+
+
+PHASES = ("route_prep", "gemm1", "gemm2", "combine")
+
+
+def phase_timing(enable: bool) -> None:
+    """Start (resetting the totals) or stop per-phase CUDA-event timing of fused calls."""
+    lib().moe_phase_timing(int(enable))
+
+
+def phase_times():
+    """(dict phase -> summed ms, number of timed calls); waits for the recorded events."""
+    ms = (ctypes.c_double * 4)()
+    calls = ctypes.c_int64(0)
+    st = lib().moe_phase_times(ms, ctypes.byref(calls))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_phase_times")
+    return {n: float(ms[i]) for i, n in enumerate(PHASES)}, int(calls.value)

@@ -14,6 +14,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/candle_moe.h"
 #include "common.cuh"
@@ -39,6 +40,32 @@ struct DeviceState {
 };
 
 DeviceState g_dev[kMaxDevices];
+
+// ---- benchmark instrumentation: kernel launch counter and per-phase CUDA events ------------
+std::atomic<int64_t> g_launches{0};
+constexpr int kPhases = 4;  // route preparation, GEMM-1, GEMM-2, combine
+struct PhaseTimer {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> events;  // kPhases + 1 per recorded call
+  int64_t calls = 0;
+};
+PhaseTimer g_timer;
+
+// Events for the next timed call (nullptr when timing is off).
+cudaEvent_t* timer_slots() {
+  std::lock_guard<std::mutex> lk(g_timer.mu);
+  if (!g_timer.on) return nullptr;
+  const size_t need = static_cast<size_t>(g_timer.calls + 1) * (kPhases + 1);
+  while (g_timer.events.size() < need) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    g_timer.events.push_back(e);
+  }
+  cudaEvent_t* slot = g_timer.events.data() + g_timer.calls * (kPhases + 1);
+  ++g_timer.calls;
+  return slot;
+}
 std::mutex g_dev_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -66,8 +93,9 @@ int init_device(int dev, DeviceState** out) {
     cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
     if (cudaMalloc(&d.err_word, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
-    route_prep_set_attributes();
-    sm100_set_attributes();
+    const bool attrs_ok = route_prep_set_attributes() && sm100_set_attributes();
+    cudaGetLastError();  // attribute failures are reported here, not by a later call
+    if (!attrs_ok) return MOE_ERR_CUDA;
     if (!g_encode) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -141,8 +169,9 @@ int finish(int status) {
 }
 
 bool sm100_shape_ok(int dtype, const void* x, const void* g, const void* u, const void* d,
-                    const void* out, int H, int I, int moe_type) {
+                    const void* out, int H, int I, int E, int moe_type) {
   if (dtype == kF32) return false;
+  if (E > sm100_max_experts()) return false;
   if (H % 128 != 0 || I % 128 != 0) return false;
   if (!aligned16(x) || !aligned16(g) || !aligned16(u) || !aligned16(out)) return false;
   if (moe_type == 0 && !aligned16(d)) return false;
@@ -168,7 +197,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
 
   const int gpath = g_gemm_path.load();
   bool use_sm100 = sm100_shape_ok(static_cast<int>(dtype), input, gate, up, down, output, H, I,
-                                  static_cast<int>(moe_type)) &&
+                                  E, static_cast<int>(moe_type)) &&
                    ds->cc_major == 10 && g_encode != nullptr;
   if (gpath == 1) use_sm100 = false;
   if (gpath == 2 && !use_sm100) return MOE_ERR_UNSUPPORTED;
@@ -201,6 +230,9 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   const int64_t rows = T * k;
   const int64_t mtile_bound = rows / bm + (E < rows ? E : rows);
   const size_t elt = dtype == kF32 ? 4 : 2;
+  cudaEvent_t* ev = timer_slots();
+  if (ev) cudaEventRecord(ev[0], stream);
+  int64_t launches = route_prep_scratch_bytes(rows, E) ? 3 : 1;
 
   st = launch_route_prep(idx, rw, T, k, E, bm, offsets, tile_prefix, s_token, s_w, s_flat,
                          prep_scratch, stream) == 0
@@ -209,6 +241,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   if (st == MOE_OK && k == 1)
     if (cudaMemsetAsync(output, 0, elt * static_cast<size_t>(T) * H, stream) != cudaSuccess)
       st = MOE_ERR_CUDA;
+  if (ev) cudaEventRecord(ev[1], stream);
 
   if (st == MOE_OK && use_sm100) {
     // GEMM-1
@@ -216,10 +249,12 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
     const int bn1 = (mode1 == kModeG1Single && I % 256 == 0) ? 256 : 128;
     const int cols1 = sm100_out_cols(mode1, bn1);
-    bool ok = make_map_2d(&mA, dtype, input, H, T, 64, 1) &&
+    // GEMM-1 gathers its A rows with cp.async; mA is an unused placeholder there
+    bool ok = make_map_2d(&mA, dtype, input, H, T, 64, 64) &&
               make_map_2d(&mB0, dtype, gate, I, static_cast<uint64_t>(E) * H, 64, 64) &&
               make_map_2d(&mB1, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 64);
     Sm100Params p;
+    p.a_rows = input;
     p.offsets = offsets;
     p.tile_prefix = tile_prefix;
     p.sorted_token = s_token;
@@ -238,6 +273,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       if (launch_sm100_gemm(static_cast<int>(dtype), mode1, bn1, mA, mB0, mB1, p, grid, stream))
         ok = false;
     }
+    if (ev) cudaEventRecord(ev[2], stream);
     // GEMM-2
     const int mode2 = moe_type == 0 ? kModeG2MN : kModeG2K;
     const int bn2 = H % 256 == 0 ? 256 : 128;
@@ -278,6 +314,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     st = launch_simt_gemm(static_cast<int>(dtype), moe_type == 0 ? 0 : 1, p, mtile_bound, stream) == 0
              ? MOE_OK
              : MOE_ERR_UNSUPPORTED;
+    if (ev) cudaEventRecord(ev[2], stream);
     if (st == MOE_OK) {
       p.a = inter;
       p.b0 = moe_type == 0 ? down : up;
@@ -291,8 +328,14 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     }
     t_last_path = 1;
   }
-  if (st == MOE_OK && k > 1)
+  if (ev) cudaEventRecord(ev[3], stream);
+  launches += 2;
+  if (st == MOE_OK && k > 1) {
     launch_combine(static_cast<int>(dtype), slot, idx, T, k, H, E, output, ds->num_sms, stream);
+    ++launches;
+  }
+  if (ev) cudaEventRecord(ev[4], stream);
+  if (st == MOE_OK) g_launches += launches;
   if (owned) cudaFreeAsync(ws, stream);
   return finish(st);
 }
@@ -333,6 +376,7 @@ CMOE_API int moe_topk_softmax_v2(const float* gating_output, float* topk_weights
                     static_cast<int>(num_tokens), topk, renormalize, ds->num_sms,
                     static_cast<cudaStream_t>(stream)) != 0)
     return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
   return finish(MOE_OK);
 }
 
@@ -370,6 +414,7 @@ CMOE_API int moe_route_prep(const uint32_t* expert_indices, const float* routing
                          scratch, s) == 0
            ? MOE_OK
            : MOE_ERR_UNSUPPORTED;
+  if (st == MOE_OK) g_launches += scratch_bytes ? 3 : 1;
   if (scratch) cudaFreeAsync(scratch, s);
   return finish(st);
 }
@@ -432,3 +477,28 @@ CMOE_API int32_t moe_set_gemm_path(int32_t path) {
 }
 
 CMOE_API int32_t moe_last_gemm_path(void) { return t_last_path; }
+
+CMOE_API int64_t moe_kernel_launches(void) { return g_launches.load(); }
+
+CMOE_API int moe_phase_timing(int32_t enable) {
+  std::lock_guard<std::mutex> lk(g_timer.mu);
+  if (enable) g_timer.calls = 0;
+  g_timer.on = enable != 0;
+  return MOE_OK;
+}
+
+CMOE_API int moe_phase_times(double* ms, int64_t* calls) {
+  std::lock_guard<std::mutex> lk(g_timer.mu);
+  for (int i = 0; i < kPhases; ++i) ms[i] = 0.0;
+  for (int64_t c = 0; c < g_timer.calls; ++c) {
+    cudaEvent_t* e = g_timer.events.data() + c * (kPhases + 1);
+    if (cudaEventSynchronize(e[kPhases]) != cudaSuccess) return MOE_ERR_CUDA;
+    for (int i = 0; i < kPhases; ++i) {
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, e[i], e[i + 1]) != cudaSuccess) return MOE_ERR_CUDA;
+      ms[i] += t;
+    }
+  }
+  if (calls) *calls = g_timer.calls;
+  return MOE_OK;
+}

@@ -163,6 +163,17 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 16-byte global -> shared copy through L2 only (cp.async.cg); completion is tracked by
+// cp_async_mbar_arrive_noinc on an mbarrier whose expected count includes this thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has completed (the arrival is
+// counted in the barrier's initial expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // tcgen05 / TMEM
 // ---------------------------------------------------------------------------------------------
@@ -247,6 +258,16 @@ __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 
 // Expert owning linear m-tile `mt`: the largest e with tile_prefix[e] <= mt.  Requires
 // 0 <= mt < tile_prefix[E] (tile_prefix is non-decreasing, tile_prefix[0] = 0).
+__device__ __forceinline__ int expert_of_tile_smem(const int32_t* tile_prefix, int E, int mt) {
+  int lo = 0, hi = E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tile_prefix[mid] <= mt) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
 __device__ __forceinline__ int expert_of_tile(const int32_t* __restrict__ tile_prefix, int E,
                                               int mt) {
   int lo = 0, hi = E;

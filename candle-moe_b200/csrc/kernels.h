@@ -15,7 +15,7 @@ int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int
 // ---- route_prep.cu ---------------------------------------------------------------------------
 size_t route_prep_scratch_bytes(int64_t rows, int E);
 int route_prep_max_experts();
-void route_prep_set_attributes();
+bool route_prep_set_attributes();
 int launch_route_prep(const uint32_t* idx, const float* wts, int64_t num_tokens, int k, int E,
                       int bm, int32_t* offsets, int32_t* tile_prefix, int32_t* s_token,
                       float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream);
@@ -49,6 +49,7 @@ enum GemmMode : int {
 };
 
 struct Sm100Params {
+  const void* a_rows;           // GEMM-1: x [T, K] (rows gathered by sorted_token); else unused
   const int32_t* offsets;       // [E+2]
   const int32_t* tile_prefix;   // [E+1], tile height sm100_tile_m()
   const int32_t* sorted_token;  // [rows]
@@ -64,8 +65,9 @@ struct Sm100Params {
 };
 int sm100_tile_m();
 int sm100_tile_k();
-size_t sm100_smem_bytes();
-void sm100_set_attributes();
+size_t sm100_smem_bytes(int num_experts);
+int sm100_max_experts();
+bool sm100_set_attributes();
 // Output columns covered by one tile of `mode` with B tile width bn (128 or 256).
 int sm100_out_cols(int mode, int bn);
 int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,

@@ -4,21 +4,25 @@
 // qwen3_moe.cu:354-966 / 1289-1903) for hidden / intermediate sizes that are multiples of the
 // tile sizes.  One CTA per SM walks the linear tile list (m-tile of an expert x n-tile), with
 // warp roles:
-//   warp 0     TMA producer.  GEMM-1 gathers the 128 token rows of an m-tile straight from x
-//              with tile::gather4 (four rows per copy, one copy per lane); GEMM-2 reads the
-//              contiguous intermediate rows with one tiled copy.  B tiles come from the expert's
-//              weights in their API layout: gate/up [E,H,I] and down [E,I,H] as MN-major
-//              operands, Nomic's up [E,H,I] as the K-major operand of h.U^T.
+//   warp 0     TMA producer (one thread).  B tiles come from the expert's weights in their API
+//              layout: gate/up [E,H,I] and down [E,I,H] as MN-major operands, Nomic's up [E,H,I]
+//              as the K-major operand of h.U^T.  GEMM-2's A (contiguous intermediate rows) is one
+//              tiled copy per stage.
+//   warps 2-3  GEMM-1's A: the 128 token rows of an m-tile are gathered from x with 16-byte
+//              cp.async copies written straight into the 128-byte-swizzled layout (a TMA
+//              tile::gather4 version of this producer measured 2-3x slower on B200), completion
+//              signalled with cp.async.mbarrier.arrive.  Warp 2 also owns the TMEM allocation.
 //   warp 1     one thread issues tcgen05.mma (M=128, N=128/256, K=16, f32 accumulate in TMEM)
 //              and tcgen05.commit to release smem stages and publish accumulators.
-//   warp 2     allocates / frees the 512 TMEM columns (two accumulator buffers of 256).
 //   warps 4-7  epilogue: tcgen05.ld the accumulator (one TMEM lane per output row), apply the
 //              fused epilogue and store 64-byte row segments:
 //                GEMM-1 Qwen3  act(g)*u  -> intermediate row (operand type)
 //                GEMM-1 Nomic  act(g)    -> intermediate row
 //                GEMM-2        acc*w     -> (token, slot) row of the slot buffer, or the output
 //                                           row itself when k = 1
-// Operands are staged with 128-byte swizzle in a 4-stage mbarrier ring (48 KB per stage).
+// Operands are staged with 128-byte swizzle in a 4-stage mbarrier ring (48 KB per stage); the
+// per-expert tile tables are copied to shared memory so that tile boundaries cost no global
+// round trips.
 // Every wait is bounded (common.cuh); a timeout sets a bit in the device error word.
 #include <stdint.h>
 
@@ -36,14 +40,22 @@ constexpr int kStageBytes = kAStageBytes + kBStageBytesMax;      // 48 KB
 constexpr int kTmemCols = 512;
 constexpr int kAccStride = 256;                                  // TMEM columns per buffer
 constexpr int kSm100Threads = 256;
-constexpr size_t kSm100Smem = static_cast<size_t>(kStages) * kStageBytes + 1024;
+constexpr int kGatherThreads = 64;                               // warps 2-3 gather A rows
+// stages + alignment slack; the tile tables (2E+3 ints) follow
+constexpr size_t kSm100SmemBase = static_cast<size_t>(kStages) * kStageBytes + 1024;
+// 227 KB opt-in limit (232448 bytes) less room for the kernel's static shared variables
+constexpr size_t kSm100SmemMax = 232448 - 1024;
 
 template <int MODE, int BN>
 struct TileCfg {
+  static constexpr bool kGather = (MODE == kModeG1Dual || MODE == kModeG1Single);
   static constexpr int kMmaN = (MODE == kModeG1Dual) ? 128 : BN;
   static constexpr int kOutCols = (MODE == kModeG1Dual) ? 128 : BN;
   static constexpr int kBBytes = (MODE == kModeG1Dual) ? 2 * 128 * kBK * 2 : BN * kBK * 2;
-  static constexpr uint32_t kTxBytes = kAStageBytes + kBBytes;
+  // bytes the TMA copies of one stage deliver (A too when it is not gathered)
+  static constexpr uint32_t kTxBytes = kBBytes + (kGather ? 0 : kAStageBytes);
+  // arrivals that complete a full barrier: the TMA thread + every gather thread
+  static constexpr uint32_t kFullCount = 1 + (kGather ? kGatherThreads : 0);
 };
 
 template <typename T> struct UmmaFmt;
@@ -54,15 +66,18 @@ struct TileInfo {
   int e, row_base, valid, n0;
 };
 
-__device__ __forceinline__ TileInfo decode_tile(const Sm100Params& p, int tile, int out_cols) {
+// tile -> (expert, first sorted row, rows present, first output column), from the shared-memory
+// copies of tile_prefix[0..E] and offsets[0..E]
+__device__ __forceinline__ TileInfo decode_tile(const int32_t* s_tp, const int32_t* s_off, int E,
+                                                int n_tiles, int tile, int out_cols) {
   TileInfo ti;
-  const int mt = tile / p.n_tiles;
-  const int nt = tile - mt * p.n_tiles;
-  ti.e = expert_of_tile(p.tile_prefix, p.E, mt);
-  const int m0 = (mt - __ldg(p.tile_prefix + ti.e)) * kBM;
-  const int off = __ldg(p.offsets + ti.e);
+  const int mt = tile / n_tiles;
+  const int nt = tile - mt * n_tiles;
+  ti.e = expert_of_tile_smem(s_tp, E, mt);
+  const int m0 = (mt - s_tp[ti.e]) * kBM;
+  const int off = s_off[ti.e];
   ti.row_base = off + m0;
-  ti.valid = min(kBM, __ldg(p.offsets + ti.e + 1) - off - m0);
+  ti.valid = min(kBM, s_off[ti.e + 1] - off - m0);
   ti.n0 = nt * out_cols;
   return ti;
 }
@@ -97,14 +112,22 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t smem_base = (raw + 1023u) & ~1023u;
+  // tile tables after the (1024-aligned) stage ring
+  int32_t* s_tp = reinterpret_cast<int32_t*>(smem_raw + (smem_base - raw) +
+                                             static_cast<size_t>(kStages) * kStageBytes);
+  int32_t* s_off = s_tp + (p.E + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total_tiles = __ldg(p.tile_prefix + p.E) * p.n_tiles;
+  const int E = p.E;
   const int num_kb = p.K / kBK;
 
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_tp[i] = __ldg(p.tile_prefix + i);
+    s_off[i] = __ldg(p.offsets + i);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_addr(&bar_full[s]), 1);
+      mbar_init(smem_addr(&bar_full[s]), C::kFullCount);
       mbar_init(smem_addr(&bar_empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -115,7 +138,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
+    if (!C::kGather) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB0);
     if (MODE == kModeG1Dual) tma_prefetch_desc(&tmB1);
   }
@@ -127,42 +150,28 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem;
+  const int total_tiles = s_tp[E] * p.n_tiles;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    uint32_t stage = 0, phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-      const TileInfo ti = decode_tile(p, tile, C::kOutCols);
-      int tok0 = 0, tok1 = 0, tok2 = 0, tok3 = 0;
-      if (MODE == kModeG1Dual || MODE == kModeG1Single) {
-        const int r = lane * 4;
-        const int last = ti.valid - 1;
-        tok0 = __ldg(p.sorted_token + ti.row_base + min(r + 0, last));
-        tok1 = __ldg(p.sorted_token + ti.row_base + min(r + 1, last));
-        tok2 = __ldg(p.sorted_token + ti.row_base + min(r + 2, last));
-        tok3 = __ldg(p.sorted_token + ti.row_base + min(r + 3, last));
-      }
-      for (int kb = 0; kb < num_kb; ++kb) {
-        bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
-                                     kErrWaitEmpty);
-        got = __all_sync(0xffffffffu, got);
-        if (!got) {
-          ok = false;
-          break;
-        }
-        const uint32_t full = smem_addr(&bar_full[stage]);
-        if (lane == 0) mbar_arrive_expect_tx(full, C::kTxBytes);
-        __syncwarp();
-        const uint32_t a_dst = smem_base + stage * kStageBytes;
-        const uint32_t b_dst = a_dst + kAStageBytes;
-        const int kc = kb * kBK;
-        if (MODE == kModeG1Dual || MODE == kModeG1Single) {
-          tma_gather4(a_dst + lane * 4 * 128, &tmA, full, kc, tok0, tok1, tok2, tok3);
-        } else if (lane == 0) {
-          tma_load_2d(a_dst, &tmA, full, kc, ti.row_base);
-        }
-        if (lane == 0) {
+    // ------------------------------------------------------------------ TMA producer (B; A too
+    // when A is a contiguous run of sorted rows)
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
+                                 kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = smem_addr(&bar_full[stage]);
+          mbar_arrive_expect_tx(full, C::kTxBytes);
+          const uint32_t a_dst = smem_base + stage * kStageBytes;
+          const uint32_t b_dst = a_dst + kAStageBytes;
+          const int kc = kb * kBK;
+          if (!C::kGather) tma_load_2d(a_dst, &tmA, full, kc, ti.row_base);
           if (MODE == kModeG1Dual) {
             const int krow = ti.e * p.K + kc;
             tma_load_2d(b_dst, &tmB0, full, ti.n0, krow);
@@ -172,14 +181,15 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           } else if (MODE == kModeG1Single || MODE == kModeG2MN) {
             const int krow = ti.e * p.K + kc;
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB0, full, ti.n0 + j * 64, krow);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 8192, &tmB0, full, ti.n0 + j * 64, krow);
           } else {
             tma_load_2d(b_dst, &tmB0, full, kc, ti.e * p.N + ti.n0);
           }
-        }
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
     }
@@ -231,15 +241,65 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         umma_commit(smem_addr(&bar_accf[buf]));
       }
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ epilogue
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------ A-row gather (GEMM-1)
+    // Thread g copies 16-byte chunk c = g%8 of rows q + 8i (q = g/8, i = 0..15) of each stage,
+    // writing them in the 128-byte-swizzled K-major layout the MMA descriptor expects (chunk c of
+    // row r lands at chunk c ^ (r % 8) = c ^ q).
+    if (C::kGather) {
+      const int g = threadIdx.x - 64;
+      const int c = g & 7;
+      const int q = g >> 3;
+      const T* x = static_cast<const T*>(p.a_rows);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
+        const T* src[16];
+        const int last = ti.valid - 1;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int tok = __ldg(p.sorted_token + ti.row_base + min(q + 8 * i, last));
+          src[i] = x + static_cast<size_t>(tok) * p.K + c * 8;
+        }
+        const uint32_t dst_off = static_cast<uint32_t>(q * 128 + ((c ^ q) << 4));
+        for (int kb = 0; kb < num_kb; ++kb) {
+          bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
+                                       kErrWaitEmpty);
+          got = __all_sync(0xffffffffu, got);
+          if (!got) {
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = smem_base + stage * kStageBytes + dst_off;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) cp_async16(a_dst + i * 8 * 128, src[i] + kb * kBK);
+          cp_async_mbar_arrive_noinc(smem_addr(&bar_full[stage]));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 4-7)
     const int q = warp - 4;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
     T* out = static_cast<T*>(p.out);
     int lt = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++lt) {
-      const TileInfo ti = decode_tile(p, tile, C::kOutCols);
+      const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
       const int buf = lt & 1;
+      const bool live = r < ti.valid;
+      int64_t orow = 0;
+      float wgt = 1.f;
+      if (C::kGather) {
+        orow = ti.row_base + r;
+      } else if (live) {
+        orow = __ldg(p.sorted_flat + ti.row_base + r);
+        wgt = __ldg(p.sorted_w + ti.row_base + r);
+      }
       bool got = mbar_wait_bounded(smem_addr(&bar_accf[buf]), static_cast<uint32_t>((lt >> 1) & 1),
                                    &s_abort, p.err, kErrWaitAccFull);
       got = __all_sync(0xffffffffu, got);
@@ -247,33 +307,24 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                           static_cast<uint32_t>(buf * kAccStride);
-      const bool live = r < ti.valid;
-      int64_t orow = 0;
-      float wgt = 1.f;
-      if (MODE == kModeG1Dual || MODE == kModeG1Single) {
-        orow = ti.row_base + r;
-      } else if (live) {
-        orow = __ldg(p.sorted_flat + ti.row_base + r);
-        wgt = __ldg(p.sorted_w + ti.row_base + r);
-      }
       T* dst_row = out + orow * p.N + ti.n0;
       if (MODE == kModeG1Dual) {
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(tb + c, g);
-          tmem_ld_32x32b_x32(tb + 128 + c, u);
+        for (int cc = 0; cc < 128; cc += 32) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tb + cc, gv);
+          tmem_ld_32x32b_x32(tb + 128 + cc, uv);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(g[i]), p.act) * __uint_as_float(u[i]);
-          if (live) store_row32<T>(dst_row + c, v);
+          for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(gv[i]), p.act) * __uint_as_float(uv[i]);
+          if (live) store_row32<T>(dst_row + cc, v);
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int cc = 0; cc < BN; cc += 32) {
           uint32_t a[32];
-          tmem_ld_32x32b_x32(tb + c, a);
+          tmem_ld_32x32b_x32(tb + cc, a);
           tmem_ld_wait();
           float v[32];
           if (MODE == kModeG1Single) {
@@ -283,7 +334,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) * wgt;
           }
-          if (live) store_row32<T>(dst_row + c, v);
+          if (live) store_row32<T>(dst_row + cc, v);
         }
       }
       tc_fence_before();
@@ -309,37 +360,47 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 
 int sm100_tile_m() { return kBM; }
 int sm100_tile_k() { return kBK; }
-size_t sm100_smem_bytes() { return kSm100Smem; }
+size_t sm100_smem_bytes(int num_experts) {
+  return kSm100SmemBase + static_cast<size_t>(2 * num_experts + 3) * sizeof(int32_t);
+}
+int sm100_max_experts() {
+  return static_cast<int>((kSm100SmemMax - kSm100SmemBase) / (2 * sizeof(int32_t))) - 2;
+}
 
 int sm100_out_cols(int mode, int bn) { return mode == kModeG1Dual ? 128 : bn; }
 
 template <typename T, int MODE, int BN>
-static void set_attr_one() {
-  cudaFuncSetAttribute(sm100_grouped_gemm_kernel<T, MODE, BN>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSm100Smem));
+static bool set_attr_one() {
+  return cudaFuncSetAttribute(sm100_grouped_gemm_kernel<T, MODE, BN>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSm100SmemMax)) == cudaSuccess;
 }
 
 template <typename T>
-static void set_attr_t() {
-  set_attr_one<T, kModeG1Dual, 128>();
-  set_attr_one<T, kModeG1Single, 128>();
-  set_attr_one<T, kModeG1Single, 256>();
-  set_attr_one<T, kModeG2MN, 128>();
-  set_attr_one<T, kModeG2MN, 256>();
-  set_attr_one<T, kModeG2K, 128>();
-  set_attr_one<T, kModeG2K, 256>();
+static bool set_attr_t() {
+  bool ok = set_attr_one<T, kModeG1Dual, 128>();
+  ok &= set_attr_one<T, kModeG1Single, 128>();
+  ok &= set_attr_one<T, kModeG1Single, 256>();
+  ok &= set_attr_one<T, kModeG2MN, 128>();
+  ok &= set_attr_one<T, kModeG2MN, 256>();
+  ok &= set_attr_one<T, kModeG2K, 128>();
+  ok &= set_attr_one<T, kModeG2K, 256>();
+  return ok;
 }
 
-void sm100_set_attributes() {
-  set_attr_t<__nv_bfloat16>();
-  set_attr_t<__half>();
+bool sm100_set_attributes() {
+  bool ok = set_attr_t<__nv_bfloat16>();
+  ok &= set_attr_t<__half>();
+  return ok;
 }
 
 template <typename T>
 static int launch_t(int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
                     const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s) {
+  const size_t smem = sm100_smem_bytes(p.E);
+  if (smem > kSm100SmemMax) return 2;
 #define CMOE_SM100(MODE, BN)                                                                 \
-  sm100_grouped_gemm_kernel<T, MODE, BN><<<grid, kSm100Threads, kSm100Smem, s>>>(a, b0, b1, p); \
+  sm100_grouped_gemm_kernel<T, MODE, BN><<<grid, kSm100Threads, smem, s>>>(a, b0, b1, p); \
   return 0;
   switch (mode) {
     case kModeG1Dual:

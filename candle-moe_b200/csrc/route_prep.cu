@@ -210,11 +210,14 @@ size_t route_prep_scratch_bytes(int64_t rows, int E) {
 int route_prep_max_experts() { return 2048; }
 
 // Once per device: allow the shared-memory sizes that large expert counts need.
-void route_prep_set_attributes() {
-  cudaFuncSetAttribute(route_prep_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(2 * 2048 + kPrepWarps * 2048) * 4);
-  cudaFuncSetAttribute(route_prep_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(2048 + kPrepWarps * 2048) * 4);
+bool route_prep_set_attributes() {
+  bool ok = cudaFuncSetAttribute(route_prep_single_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(2 * 2048 + kPrepWarps * 2048) * 4) == cudaSuccess;
+  ok &= cudaFuncSetAttribute(route_prep_scatter_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(2048 + kPrepWarps * 2048) * 4) == cudaSuccess;
+  return ok;
 }
 
 // scratch: route_prep_scratch_bytes() bytes (may be null when that is 0).

@@ -137,6 +137,21 @@ int32_t moe_set_gemm_path(int32_t path);
  * cores, 0 none. */
 int32_t moe_last_gemm_path(void);
 
+/*
+ * Benchmark instrumentation (counterpart of the NVTX ranges the reference's profiling binary
+ * puts around each forward, src/bin/profile_fused_moe.rs:109-127).
+ *
+ * moe_kernel_launches: kernels this library has launched so far in this process.
+ * moe_phase_timing(1): from now on every moe_fused_v2 / fused_moe call records CUDA events on
+ *   its stream around route preparation, GEMM-1, GEMM-2 and the combine (resets the totals);
+ *   moe_phase_timing(0) stops recording.
+ * moe_phase_times: waits for the recorded events and writes the summed milliseconds of the four
+ *   phases to ms[0..3] and the number of recorded calls to *calls.
+ */
+int64_t moe_kernel_launches(void);
+int moe_phase_timing(int32_t enable);
+int moe_phase_times(double* ms, int64_t* calls);
+
 #ifdef __cplusplus
 }
 #endif

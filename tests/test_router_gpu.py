@@ -57,9 +57,11 @@ def test_drop_in_apply_topk_softmax_inplace_uint32():
     idx = torch.zeros(8, 2, dtype=torch.uint32, device="cuda")
     src = torch.zeros(8, 2, dtype=torch.uint32, device="cuda")
     candle_moe.apply_topk_softmax_inplace(logits, w, idx, src)
-    p = torch.softmax(logits.double(), -1)
+    p = torch.softmax(logits, -1)  # f32, as candle's softmax_last_dim in the reference test
     v, i = torch.topk(p, 2)
-    assert np.array_equal(np.round(w.cpu().numpy(), 3), np.round(v.cpu().numpy(), 3))
+    # the reference test rounds both to 3 decimals; a 1-ulp difference can straddle a rounding
+    # boundary, so compare the unrounded values at f32 resolution instead
+    assert np.abs(w.cpu().numpy() - v.cpu().numpy()).max() <= 1e-6
     assert np.array_equal(idx.cpu().numpy().astype(np.int64), i.cpu().numpy())
     assert np.array_equal(src.cpu().numpy().astype(np.int64),
                           np.arange(2)[None, :] * 8 + np.arange(8)[:, None])
