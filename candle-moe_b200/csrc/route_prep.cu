@@ -18,6 +18,11 @@
 // of at most kPrepRows rows run all three phases in one CTA.
 #include <stdint.h>
 
+#include <atomic>
+#include <climits>
+#include <mutex>
+
+#include "../../include/candle_moe.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -246,4 +251,85 @@ int launch_route_prep(const uint32_t* idx, const float* wts, int64_t num_tokens,
   return 0;
 }
 
+
+// ---- route preparation without allocation ---------------------------------------------------
+//
+// Some callers cannot allocate device memory while they run this step: a serving loop whose
+// allocator owns every byte of HBM and forbids side allocations, a framework plugin that is
+// handed its buffers and must not call cudaMalloc, or code that records the step into a CUDA
+// graph.  moe_route_prep_noalloc serves them: its scratch (the per-block histograms and block
+// bases of the multi-block path, 2 * ceil(T*k / 4096) * E ints) lives in the fixed device array
+// below, which every GPU that loads this library holds until the process exits.  Requests whose
+// scratch would not fit are rejected with MOE_ERR_WORKSPACE before anything is launched.
+//
+// All calls share the one array.  Each call overwrites every scratch entry it later reads (the
+// count kernel writes all histograms, the scan all bases), so nothing has to start at zero, but
+// two calls that overlap on the GPU (different streams, or host threads racing on one device)
+// race on the array: serialise them, e.g. on one stream.
+//
+// The first call on each device performs the set-up (it resolves the array's device address with
+// cudaGetSymbolAddress and sets the kernels' shared-memory attributes, with that device current);
+// make that first call before any stream capture begins.
+
+constexpr int kNoAllocScratchInts = 1 << 19;  // 2 MiB
+static __device__ __align__(256) int32_t g_route_prep_noalloc_scratch[kNoAllocScratchInts];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::atomic<int32_t*> g_noalloc_ptr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device (set up on first use).
+int32_t* noalloc_scratch_current_device(int* status) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    cudaGetLastError();
+    *status = MOE_ERR_CUDA;
+    return nullptr;
+  }
+  int32_t* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  p = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_route_prep_noalloc_scratch);
+    if (e != cudaSuccess || addr == nullptr) {
+      cudaGetLastError();
+      *status = MOE_ERR_CUDA;
+      return nullptr;
+    }
+    if (!route_prep_set_attributes()) {
+      cudaGetLastError();
+      *status = MOE_ERR_CUDA;
+      return nullptr;
+    }
+    p = static_cast<int32_t*>(addr);
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+}  // namespace
+
 }  // namespace cmoe
+
+extern "C" __attribute__((visibility("default"))) int moe_route_prep_noalloc(
+    const uint32_t* expert_indices, const float* routing_weights, int64_t num_tokens,
+    int32_t topk, int32_t num_experts, int32_t* expert_offsets, int32_t* sorted_token_ids,
+    float* sorted_weights, void* stream) {
+  using namespace cmoe;
+  if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
+  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
+    return MOE_ERR_UNSUPPORTED;
+  const size_t need = route_prep_scratch_bytes(num_tokens * topk, num_experts);
+  if (need > sizeof(int32_t) * static_cast<size_t>(kNoAllocScratchInts)) return MOE_ERR_WORKSPACE;
+  int status = MOE_OK;
+  int32_t* scratch = noalloc_scratch_current_device(&status);
+  if (!scratch) return status;
+  if (launch_route_prep(expert_indices, routing_weights, num_tokens, topk, num_experts, 1,
+                        expert_offsets, nullptr, sorted_token_ids, sorted_weights, nullptr,
+                        scratch, static_cast<cudaStream_t>(stream)) != 0)
+    return MOE_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}

@@ -152,6 +152,23 @@ int64_t moe_kernel_launches(void);
 int moe_phase_timing(int32_t enable);
 int moe_phase_times(double* ms, int64_t* calls);
 
+/*
+ * moe_route_prep without any allocation.  This entry point has no counterpart in the reference.
+ * It exists for callers that cannot allocate device memory during the step (an allocator that
+ * owns all of HBM, a plugin handed only its buffers, a graph being recorded): instead of the pool,
+ * its scratch is a fixed 2 MiB device array built into the library, held by every GPU that loads
+ * the library until the process exits.  Same arguments, outputs and statuses as moe_route_prep;
+ * requests needing more scratch than the array holds (2 * ceil(num_tokens * topk / 4096) *
+ * num_experts > 524288 ints, e.g. more than 8,388,608 routed rows at 128 experts) return
+ * MOE_ERR_WORKSPACE without launching anything.  All calls share the array, so calls that overlap
+ * on the GPU race: serialise them (one stream).  The first call on a device sets it up (resolves
+ * the array's address with that device current); make it before any stream capture.
+ */
+int moe_route_prep_noalloc(const uint32_t* expert_indices, const float* routing_weights,
+                           int64_t num_tokens, int32_t topk, int32_t num_experts,
+                           int32_t* expert_offsets, int32_t* sorted_token_ids,
+                           float* sorted_weights, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
