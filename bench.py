@@ -10,9 +10,11 @@ so no explicit flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1..c5]
 
-N>1 (torchrun, one rank per GPU): each rank runs its own replica of the workload (the
-expert-parallel exchange is not in this version), value = tokens of all ranks / max-over-ranks
-time.  --impl reference times the reference's algorithm on the host cores (the CPU oracle port,
+N>1 (torchrun, one rank per GPU), config 5: expert parallel -- every rank holds 65536 tokens and
+128/N experts; tokens are dispatched to the ranks owning their experts and the weighted
+contributions returned with NCCL all_to_all_single (candle-moe_b200/expert_parallel.py); weak
+scaling, value = tokens of all ranks / max-over-ranks step time.  Other configs run one replica
+per rank.  --impl reference times the reference's algorithm on the host cores (the CPU oracle port,
 all threads) on a bounded token sample per step; the reference crate has no CPU implementation
 of its own and its CUDA GEMM kernels cannot launch at these sizes.
 """
@@ -143,23 +145,27 @@ def max_over_ranks(world, value):
     return float(t.item())
 
 
-def make_inputs(cfg, seed=0):
-    """Seeded synthetic inputs on the current GPU."""
+def make_inputs(cfg, seed=0, rank=0, n_local_experts=None):
+    """Seeded synthetic inputs on the current GPU: this rank's tokens and, with expert
+    parallelism, only its n_local_experts experts."""
     import torch
     dtype, moe_type, act, T, H, I, E, k, renorm, bias_std = cfg
+    El = E if n_local_experts is None else n_local_experts
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    bias = torch.randn(E, generator=g, device="cuda") * bias_std  # the router bias is global
+    g.manual_seed(seed * 1000 + rank)
     logits = torch.randn(T, E, generator=g, device="cuda")
     if bias_std:
-        logits += torch.randn(E, generator=g, device="cuda") * bias_std
+        logits += bias
     inp = {"logits": logits}
     if moe_type is None:
         return inp
     inp["x"] = torch.randn(T, H, generator=g, device="cuda").to(tdt)
-    inp["gate"] = (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(tdt)
-    inp["up"] = (torch.randn(E, H, I, generator=g, device="cuda") * 0.02).to(tdt)
-    inp["down"] = ((torch.randn(E, I, H, generator=g, device="cuda") * 0.02).to(tdt)
+    inp["gate"] = (torch.randn(El, H, I, generator=g, device="cuda") * 0.02).to(tdt)
+    inp["up"] = (torch.randn(El, H, I, generator=g, device="cuda") * 0.02).to(tdt)
+    inp["down"] = ((torch.randn(El, I, H, generator=g, device="cuda") * 0.02).to(tdt)
                    if moe_type == 0 else None)
     return inp
 
@@ -170,8 +176,15 @@ def run_ours(args, world, rank, local):
 
     cfg = CONFIGS[args.config]
     dtype, moe_type, act, T, H, I, E, k, renorm, _ = cfg
-    inp = make_inputs(cfg, seed=0)
     router_only = moe_type is None
+    ep = world > 1 and not router_only and args.config == "c5"
+    layer = None
+    if ep:
+        import expert_parallel
+        layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act))
+        inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
+    else:
+        inp = make_inputs(cfg, seed=0, rank=rank)
     moe = None if router_only else candle_moe.FusedMoE(E, k, candle_moe.Activation(act))
     stream = torch.cuda.current_stream()
 
@@ -179,6 +192,8 @@ def run_ours(args, world, rank, local):
         w, idx, _ = candle_moe.topk_softmax(logits, k, renormalize=renorm)
         if router_only:
             return w
+        if ep:
+            return layer.forward(x, inp["gate"], inp["up"], inp["down"], w, idx, moe_type)
         return moe.forward(x, inp["gate"], inp["up"], inp["down"], w, idx, moe_type)
 
     x_dev = None if router_only else inp["x"]
@@ -191,6 +206,8 @@ def run_ours(args, world, rank, local):
     clocks.start()
     launches0 = candle_moe.kernel_launches()
     candle_moe.phase_timing(True)
+    if ep:
+        layer.timing = True
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -201,6 +218,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     candle_moe.phase_timing(False)
+    if ep:
+        layer.timing = False
     clk = clocks.stop()
     ms_total = ev0.elapsed_time(ev1)
     launches = candle_moe.kernel_launches() - launches0
@@ -246,7 +265,8 @@ def run_ours(args, world, rank, local):
         "dtype": dtype, "data": "synthetic (seeded torch.randn; weights N(0,0.02), hidden N(0,1))",
         "config": {"workload": WORKLOAD_NAMES[args.config], "tokens": T, "hidden": H,
                    "intermediate": I, "experts": E, "top_k": k,
-                   "parallelism": "replicas" if world > 1 else "single-gpu",
+                   "parallelism": (f"ep{world}" if ep else "replicas") if world > 1 else "single-gpu",
+                   "tokens_per_rank": T,
                    "l2": "inputs larger than L2 (weights 1.2 GB + activations), no flush"
                    if args.config == "c5" else "no flush"},
         "gpu_launches": launches,
@@ -254,8 +274,12 @@ def run_ours(args, world, rank, local):
     }
     if router_only:
         line["value"] = ms_step * 1e3
+    if ep:
+        st, n = layer.stage_times()
+        line["ep_stages_ms"] = {s_: v / max(n, 1) for s_, v in st.items()}
+        line["ep_rows"] = layer.last_stats
     if not router_only and ncalls:
-        rows = T * k
+        rows = layer.last_stats["received_rows"] if ep else T * k
         n_up = 2 if moe_type == 0 else 1
         flops = {"gemm1": 2.0 * rows * H * I * n_up, "gemm2": 2.0 * rows * I * H}
         per_call = {p: phases[p] / ncalls for p in phases}

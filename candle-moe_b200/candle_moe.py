@@ -72,6 +72,12 @@ def lib() -> ctypes.CDLL:
         L.moe_set_gemm_path.restype = I32
         L.moe_last_gemm_path.argtypes = []
         L.moe_last_gemm_path.restype = I32
+        L.moe_route_prep_ex.argtypes = [P, P, I64, I32, I32, P, P, P, P, P]
+        L.moe_route_prep_ex.restype = ctypes.c_int
+        L.moe_gather_rows.argtypes = [P, P, I64, I32, U32, P, P]
+        L.moe_gather_rows.restype = ctypes.c_int
+        L.moe_combine_rows.argtypes = [P, P, I64, I64, I32, I32, U32, P, P]
+        L.moe_combine_rows.restype = ctypes.c_int
         L.moe_kernel_launches.argtypes = []
         L.moe_kernel_launches.restype = I64
         L.moe_phase_timing.argtypes = [I32]
@@ -203,6 +209,63 @@ def route_prep(expert_indices: torch.Tensor, routing_weights: torch.Tensor, num_
     if st != MOE_OK:
         raise MoeError(st, "moe_route_prep")
     return offsets, st_ids[:T * k], st_w[:T * k]
+
+
+def route_prep_ex(expert_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int):
+    """route_prep that also returns sorted_flat (t*k + j of each sorted row): (offsets [E+2],
+    sorted_token [T*k], sorted_weight [T*k], sorted_flat [T*k])."""
+    _need_cuda(expert_indices, "expert_indices")
+    _need_contig(expert_indices, "expert_indices")
+    _need_contig(routing_weights, "routing_weights")
+    T, k = expert_indices.shape
+    dev = expert_indices.device
+    n = max(T * k, 1)
+    offsets = torch.empty((num_experts + 2,), dtype=torch.int32, device=dev)
+    st_ids = torch.empty((n,), dtype=torch.int32, device=dev)
+    st_w = torch.empty((n,), dtype=torch.float32, device=dev)
+    st_f = torch.empty((n,), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_route_prep_ex(_ptr(expert_indices), _ptr(routing_weights), T, k,
+                                     num_experts, _ptr(offsets), _ptr(st_ids), _ptr(st_w),
+                                     _ptr(st_f), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_route_prep_ex")
+    return offsets, st_ids[:T * k], st_w[:T * k], st_f[:T * k]
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor, out: Optional[torch.Tensor] = None):
+    """out[r] = src[index[r]] (index int32, on the GPU)."""
+    _need_contig(src, "src")
+    _need_contig(index, "index")
+    rows, H = index.numel(), src.shape[1]
+    if out is None:
+        out = torch.empty((rows, H), dtype=src.dtype, device=src.device)
+    with torch.cuda.device(src.device):
+        st = lib().moe_gather_rows(_ptr(src), _ptr(index), rows, H,
+                                   fused_moe_internal_dtype(src.dtype), _ptr(out),
+                                   _stream(src.device))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_gather_rows")
+    return out
+
+
+def combine_rows(rows_buf: torch.Tensor, sorted_flat: torch.Tensor, num_tokens: int, top_k: int,
+                 out: Optional[torch.Tensor] = None):
+    """out[t] = sum over slots j of rows_buf[r] where sorted_flat[r] == t*top_k + j, in slot
+    order, f32 accumulation, one rounding."""
+    _need_contig(rows_buf, "rows_buf")
+    _need_contig(sorted_flat, "sorted_flat")
+    rows, H = rows_buf.shape
+    dev = rows_buf.device
+    if out is None:
+        out = torch.empty((num_tokens, H), dtype=rows_buf.dtype, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_combine_rows(_ptr(rows_buf), _ptr(sorted_flat), rows, num_tokens, top_k, H,
+                                    fused_moe_internal_dtype(rows_buf.dtype), _ptr(out),
+                                    _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_combine_rows")
+    return out
 
 
 # ---------------------------------------------------------------------------------------------

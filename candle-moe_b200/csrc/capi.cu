@@ -419,6 +419,78 @@ CMOE_API int moe_route_prep(const uint32_t* expert_indices, const float* routing
   return finish(st);
 }
 
+CMOE_API int moe_route_prep_ex(const uint32_t* expert_indices, const float* routing_weights,
+                               int64_t num_tokens, int32_t topk, int32_t num_experts,
+                               int32_t* expert_offsets, int32_t* sorted_token_ids,
+                               float* sorted_weights, int32_t* sorted_flat, void* stream) {
+  if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
+  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
+    return MOE_ERR_UNSUPPORTED;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t scratch_bytes = route_prep_scratch_bytes(num_tokens * topk, num_experts);
+  void* scratch = nullptr;
+  if (scratch_bytes) {
+    if (cudaMallocFromPoolAsync(&scratch, scratch_bytes, ds->pool, s) != cudaSuccess) {
+      cudaGetLastError();
+      return MOE_ERR_NO_MEMORY;
+    }
+  }
+  st = launch_route_prep(expert_indices, routing_weights, num_tokens, topk, num_experts, 1,
+                         expert_offsets, nullptr, sorted_token_ids, sorted_weights, sorted_flat,
+                         scratch, s) == 0
+           ? MOE_OK
+           : MOE_ERR_UNSUPPORTED;
+  if (st == MOE_OK) g_launches += scratch_bytes ? 3 : 1;
+  if (scratch) cudaFreeAsync(scratch, s);
+  return finish(st);
+}
+
+CMOE_API int moe_gather_rows(const void* src, const int32_t* index, int64_t rows,
+                             int32_t hidden_dim, uint32_t dtype, void* dst, void* stream) {
+  if (rows < 0 || hidden_dim <= 0 || dtype > 2) return MOE_ERR_INVALID_ARG;
+  if (rows == 0) return MOE_OK;
+  if (!src || !index || !dst) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  launch_gather_rows(static_cast<int>(dtype), src, index, rows, hidden_dim, dst, ds->num_sms,
+                     static_cast<cudaStream_t>(stream));
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, int64_t rows,
+                              int64_t num_tokens, int32_t topk, int32_t hidden_dim,
+                              uint32_t dtype, void* output, void* stream) {
+  if (rows < 0 || num_tokens < 0 || topk <= 0 || hidden_dim <= 0 || dtype > 2)
+    return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MOE_OK;
+  if (!output || (rows > 0 && (!rows_buf || !sorted_flat))) return MOE_ERR_INVALID_ARG;
+  if (rows > num_tokens * topk) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* inv = nullptr;
+  if (cudaMallocFromPoolAsync(&inv, sizeof(int32_t) * static_cast<size_t>(num_tokens) * topk,
+                              ds->pool, s) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_NO_MEMORY;
+  }
+  st = launch_combine_indirect(static_cast<int>(dtype), rows_buf, sorted_flat, rows, num_tokens,
+                               topk, hidden_dim, static_cast<int32_t*>(inv), output, ds->num_sms,
+                               s) == 0
+           ? MOE_OK
+           : MOE_ERR_CUDA;
+  if (st == MOE_OK) g_launches += rows > 0 ? 2 : 1;
+  cudaFreeAsync(inv, s);
+  return finish(st);
+}
+
 CMOE_API size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim,
                                          int32_t intermediate_dim, int32_t num_experts,
                                          int32_t topk, uint32_t moe_type, uint32_t dtype) {

@@ -38,6 +38,11 @@ int launch_simt_gemm(int dtype, int mode, const SimtParams& p, int64_t mtile_bou
                      cudaStream_t s);
 int launch_combine(int dtype, const void* slot, const uint32_t* idx, int64_t num_tokens, int k,
                    int H, int E, void* out, int num_sms, cudaStream_t s);
+int launch_gather_rows(int dtype, const void* src, const int32_t* index, int64_t rows, int H,
+                       void* dst, int num_sms, cudaStream_t s);
+int launch_combine_indirect(int dtype, const void* rows_buf, const int32_t* flat, int64_t rows,
+                            int64_t num_tokens, int k, int H, int32_t* inv, void* out,
+                            int num_sms, cudaStream_t s);
 
 // ---- moe_sm100.cu ----------------------------------------------------------------------------
 // GEMM modes shared by both grouped-GEMM families

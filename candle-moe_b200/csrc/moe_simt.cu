@@ -234,4 +234,133 @@ int launch_combine(int dtype, const void* slot, const uint32_t* idx, int64_t num
   return 0;
 }
 
+// ---- row movement for the expert-parallel exchange ------------------------------------------
+
+// dst[r, :] = src[index[r], :], 16 bytes per thread where the row allows it.
+template <typename V>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const V* __restrict__ src,
+                                                          const int32_t* __restrict__ index,
+                                                          int64_t rows, int vec_per_row,
+                                                          V* __restrict__ dst) {
+  const int64_t total = rows * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = v / vec_per_row;
+    const int c = static_cast<int>(v - r * vec_per_row);
+    dst[v] = src[static_cast<int64_t>(__ldg(index + r)) * vec_per_row + c];
+  }
+}
+
+// inv[flat[r]] = r for r < rows (inv pre-filled with -1 by the caller)
+__global__ void __launch_bounds__(256) invert_rows_kernel(const int32_t* __restrict__ flat,
+                                                          int64_t rows, int32_t* __restrict__ inv) {
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    inv[__ldg(flat + r)] = static_cast<int32_t>(r);
+}
+
+// out[t, :] = sum over slots j (in slot order) with inv[t*k+j] >= 0 of rows_buf[inv[t*k+j], :],
+// accumulated in f32 and rounded once -- the slot-ordered combine of combine_slots_kernel with
+// one indirection, for contributions that come back from other ranks in exchange order.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) combine_indirect_kernel(const T* __restrict__ rows_buf,
+                                                               const int32_t* __restrict__ inv,
+                                                               int64_t num_tokens, int k, int H,
+                                                               T* __restrict__ out) {
+  const int vec_per_row = H / V;
+  const int64_t total = num_tokens * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = v / vec_per_row;
+    const int c = static_cast<int>(v - t * vec_per_row) * V;
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int32_t r = __ldg(inv + t * k + j);
+      if (r < 0) continue;
+      const T* src = rows_buf + static_cast<int64_t>(r) * H + c;
+      if (V * sizeof(T) == 16) {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
+        const T* qe = reinterpret_cast<const T*>(&q);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(src[i]);
+      }
+    }
+    T* dst = out + t * H + c;
+    if (V * sizeof(T) == 16) {
+      uint4 q;
+      T* qe = reinterpret_cast<T*>(&q);
+#pragma unroll
+      for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
+      *reinterpret_cast<uint4*>(dst) = q;
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) dst[i] = Elem<T>::from_f(acc[i]);
+    }
+  }
+}
+
+static unsigned grid_for(int64_t work, int num_sms) {
+  int64_t blocks = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<unsigned>(blocks);
+}
+
+int launch_gather_rows(int dtype, const void* src, const int32_t* index, int64_t rows, int H,
+                       void* dst, int num_sms, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const size_t row_bytes = static_cast<size_t>(H) * (dtype == kF32 ? 4 : 2);
+  if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(src) % 16) == 0 &&
+      (reinterpret_cast<uintptr_t>(dst) % 16) == 0) {
+    const int vpr = static_cast<int>(row_bytes / 16);
+    gather_rows_kernel<uint4><<<grid_for(rows * vpr, num_sms), 256, 0, s>>>(
+        static_cast<const uint4*>(src), index, rows, vpr, static_cast<uint4*>(dst));
+  } else if (row_bytes % 4 == 0) {
+    const int vpr = static_cast<int>(row_bytes / 4);
+    gather_rows_kernel<uint32_t><<<grid_for(rows * vpr, num_sms), 256, 0, s>>>(
+        static_cast<const uint32_t*>(src), index, rows, vpr, static_cast<uint32_t*>(dst));
+  } else {
+    const int vpr = static_cast<int>(row_bytes / 2);
+    gather_rows_kernel<uint16_t><<<grid_for(rows * vpr, num_sms), 256, 0, s>>>(
+        static_cast<const uint16_t*>(src), index, rows, vpr, static_cast<uint16_t*>(dst));
+  }
+  return 0;
+}
+
+template <typename T>
+static void combine_indirect_t(const void* rows_buf, const int32_t* inv, int64_t T_, int k, int H,
+                               void* out, int num_sms, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = (H % V) == 0 && (reinterpret_cast<uintptr_t>(rows_buf) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+  if (vec)
+    combine_indirect_kernel<T, V><<<grid_for(T_ * (H / V), num_sms), 256, 0, s>>>(
+        static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+  else
+    combine_indirect_kernel<T, 1><<<grid_for(T_ * H, num_sms), 256, 0, s>>>(
+        static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+}
+
+// inv: caller scratch of num_tokens*k int32.
+int launch_combine_indirect(int dtype, const void* rows_buf, const int32_t* flat, int64_t rows,
+                            int64_t num_tokens, int k, int H, int32_t* inv, void* out,
+                            int num_sms, cudaStream_t s) {
+  if (num_tokens <= 0) return 0;
+  if (cudaMemsetAsync(inv, 0xff, sizeof(int32_t) * static_cast<size_t>(num_tokens) * k, s) !=
+      cudaSuccess)
+    return 3;
+  if (rows > 0)
+    invert_rows_kernel<<<grid_for(rows, num_sms), 256, 0, s>>>(flat, rows, inv);
+  if (dtype == kF32) combine_indirect_t<float>(rows_buf, inv, num_tokens, k, H, out, num_sms, s);
+  else if (dtype == kBF16) combine_indirect_t<__nv_bfloat16>(rows_buf, inv, num_tokens, k, H, out, num_sms, s);
+  else combine_indirect_t<__half>(rows_buf, inv, num_tokens, k, H, out, num_sms, s);
+  return 0;
+}
+
 }  // namespace cmoe

@@ -75,9 +75,20 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
 #pragma unroll
     for (int i = 0; i < kVpt; ++i) v[i] = v[i] * rs;
 
-    // k rounds of group argmax
+    // k rounds of group argmax.  Pick j is kept by lane j % TPR of the group (slot j / TPR) so
+    // that the k results leave in one coalesced store per output array; rows with more picks
+    // than the group has slots fall back to the group leader writing each pick as it is made.
+    constexpr int kSlots = 4;
+    const bool staged = k <= kSlots * kTpr;
     const int col0 = g * kElts;
     float wsum = 0.f;
+    float pw[kSlots];
+    int pe[kSlots];
+#pragma unroll
+    for (int s2 = 0; s2 < kSlots; ++s2) {
+      pw[s2] = 0.f;
+      pe[s2] = 0;
+    }
     for (int j = 0; j < k; ++j) {
       float best = v[0];
       int be = col0;
@@ -102,7 +113,16 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
         }
       }
       wsum += best;
-      if (active && g == 0) {
+      if (staged) {
+        if (j % kTpr == g) {
+#pragma unroll
+          for (int s2 = 0; s2 < kSlots; ++s2)
+            if (s2 == j / kTpr) {
+              pw[s2] = best;
+              pe[s2] = be;
+            }
+        }
+      } else if (active && g == 0) {
         const int64_t o = row * k + j;
         out_w[o] = best;
         out_idx[o] = be;
@@ -119,7 +139,20 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
             if (ll == l && ii == i) v[ll * kElts + ii] = -10000.f;
       }
     }
-    if (renorm && active && g == 0) {
+    if (staged) {
+      if (active) {
+#pragma unroll
+        for (int s2 = 0; s2 < kSlots; ++s2) {
+          const int j = s2 * kTpr + g;
+          if (j < k) {
+            const int64_t o = row * k + j;
+            out_w[o] = renorm ? pw[s2] / wsum : pw[s2];
+            out_idx[o] = pe[s2];
+            out_src[o] = static_cast<int32_t>(static_cast<int64_t>(j) * num_tokens + row);
+          }
+        }
+      }
+    } else if (renorm && active && g == 0) {
       for (int j = 0; j < k; ++j) out_w[row * k + j] = out_w[row * k + j] / wsum;
     }
   }

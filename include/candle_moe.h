@@ -102,6 +102,35 @@ int moe_route_prep(const uint32_t* expert_indices, const float* routing_weights,
                    int64_t num_tokens, int32_t topk, int32_t num_experts, int32_t* expert_offsets,
                    int32_t* sorted_token_ids, float* sorted_weights, void* stream);
 
+/*
+ * moe_route_prep that also returns, for every sorted row, its flat index t*topk + j
+ * (sorted_flat, [num_tokens * topk] i32).  Any of sorted_token_ids, sorted_weights and
+ * sorted_flat may be NULL.  Used to bucket (token, slot) rows by destination rank in the
+ * expert-parallel layer (no counterpart in the reference, which has no multi-GPU path).
+ */
+int moe_route_prep_ex(const uint32_t* expert_indices, const float* routing_weights,
+                      int64_t num_tokens, int32_t topk, int32_t num_experts,
+                      int32_t* expert_offsets, int32_t* sorted_token_ids, float* sorted_weights,
+                      int32_t* sorted_flat, void* stream);
+
+/*
+ * dst[r, :] = src[index[r], :] for r < rows; rows of hidden_dim elements of `dtype`.  The row
+ * gather of the expert-parallel dispatch (no counterpart in the reference).
+ */
+int moe_gather_rows(const void* src, const int32_t* index, int64_t rows, int32_t hidden_dim,
+                    uint32_t dtype, void* dst, void* stream);
+
+/*
+ * Slot-ordered combine of contributions that arrive in exchange order: with sorted_flat[r] the
+ * flat index t*topk + j of row r of rows_buf (r < rows), output[t, :] = sum over j (in slot
+ * order) of rows_buf[r(t,j), :], accumulated in f32 and rounded once to `dtype`; slots with no
+ * row contribute nothing.  The expert-parallel counterpart of the reference's weighted
+ * scatter-add into the output (qwen3_moe.cu:637-641).
+ */
+int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, int64_t rows,
+                     int64_t num_tokens, int32_t topk, int32_t hidden_dim, uint32_t dtype,
+                     void* output, void* stream);
+
 /* Bytes of caller workspace that moe_fused_v2 needs for these sizes (0 for num_tokens == 0). */
 size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim, int32_t intermediate_dim,
                                 int32_t num_experts, int32_t topk, uint32_t moe_type,

@@ -1,0 +1,28 @@
+"""Expert-parallel config-5-shaped layer on 2 GPUs over NCCL vs the single-GPU fused path on the
+same tokens: bit-identical (same tile math, rounding points and slot order)."""
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import ep_worker
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+@pytest.mark.parametrize("moe_type", [0, 1])
+def test_expert_parallel_two_gpus_bit_identical(moe_type):
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = ep_worker.free_port()
+    procs = [ctx.Process(target=ep_worker.gpu_rank,
+                         args=(r, 2, port, 3000, 256, 256, 16, 8, moe_type, "bf16", q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0, p.exitcode
+    for rank, same, diff, stats in sorted(q.get() for _ in range(2)):
+        assert same, (rank, diff, stats)
