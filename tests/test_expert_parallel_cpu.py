@@ -1,7 +1,7 @@
 """Expert-parallel exchange logic on two CPU ranks (gloo): bucketing by destination rank,
 all_to_all_single of counts / rows / metadata, the return trip and the slot-ordered combine,
 with the oracle standing in for the GPU compute.  The result must equal the single-process
-oracle exactly (f32, same per-row arithmetic, same slot order)."""
+oracle up to f32 reassociation (each rank sums its slots before the origin sums the ranks)."""
 import multiprocessing as pymp
 
 import pytest
@@ -24,5 +24,5 @@ def test_expert_parallel_matches_single_process_on_gloo(moe_type):
         assert p.exitcode == 0, p.exitcode
     results = sorted(q.get() for _ in range(2))
     for rank, maxdiff, stats in results:
-        assert maxdiff == 0.0, (rank, maxdiff)
-        assert stats["sent_rows"] > 0 and stats["received_rows"] > 0
+        assert maxdiff < 1e-5, (rank, maxdiff)
+        assert stats["unique_rows_sent"] > 0 and stats["rows_received"] > 0

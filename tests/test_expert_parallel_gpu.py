@@ -1,5 +1,6 @@
 """Expert-parallel config-5-shaped layer on 2 GPUs over NCCL vs the single-GPU fused path on the
-same tokens: bit-identical (same tile math, rounding points and slot order)."""
+same tokens, within the bf16 tolerance (1e-2 relative): the only difference is that each rank's
+slots are summed and rounded before the ranks' partials are summed."""
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -12,7 +13,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 @pytest.mark.parametrize("moe_type", [0, 1])
-def test_expert_parallel_two_gpus_bit_identical(moe_type):
+def test_expert_parallel_two_gpus_matches_single_gpu(moe_type):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = ep_worker.free_port()
@@ -24,5 +25,5 @@ def test_expert_parallel_two_gpus_bit_identical(moe_type):
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0, p.exitcode
-    for rank, same, diff, stats in sorted(q.get() for _ in range(2)):
-        assert same, (rank, diff, stats)
+    for rank, ok, diff, stats in sorted(q.get() for _ in range(2)):
+        assert ok, (rank, diff, stats)
