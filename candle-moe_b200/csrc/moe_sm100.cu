@@ -41,8 +41,10 @@ constexpr int kTmemCols = 512;
 constexpr int kAccStride = 256;                                  // TMEM columns per buffer
 constexpr int kSm100Threads = 256;
 constexpr int kGatherThreads = 64;                               // warps 2-3 gather A rows
-// stages + alignment slack; the tile tables (2E+3 ints) follow
-constexpr size_t kSm100SmemBase = static_cast<size_t>(kStages) * kStageBytes + 1024;
+constexpr int kStageOutBytes = 4 * 4096;                         // epilogue staging, 4 KB/warp
+// stages + alignment slack + epilogue staging; the tile tables (2E+3 ints) follow
+constexpr size_t kSm100SmemBase =
+    static_cast<size_t>(kStages) * kStageBytes + 1024 + kStageOutBytes;
 // 227 KB opt-in limit (232448 bytes) less room for the kernel's static shared variables
 constexpr size_t kSm100SmemMax = 232448 - 1024;
 
@@ -112,9 +114,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t smem_base = (raw + 1023u) & ~1023u;
-  // tile tables after the (1024-aligned) stage ring
+  // epilogue staging, then the tile tables, after the (1024-aligned) stage ring
+  const uint32_t stage_out_base = smem_base + static_cast<uint32_t>(kStages * kStageBytes);
   int32_t* s_tp = reinterpret_cast<int32_t*>(smem_raw + (smem_base - raw) +
-                                             static_cast<size_t>(kStages) * kStageBytes);
+                                             static_cast<size_t>(kStages) * kStageBytes +
+                                             kStageOutBytes);
   int32_t* s_off = s_tp + (p.E + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -307,35 +311,76 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                           static_cast<uint32_t>(buf * kAccStride);
-      T* dst_row = out + orow * p.N + ti.n0;
-      if (MODE == kModeG1Dual) {
-#pragma unroll 1
-        for (int cc = 0; cc < 128; cc += 32) {
-          uint32_t gv[32], uv[32];
-          tmem_ld_32x32b_x32(tb + cc, gv);
-          tmem_ld_32x32b_x32(tb + 128 + cc, uv);
-          tmem_ld_wait();
-          float v[32];
+      // Stores go through a 4 KB per-warp staging buffer (32 rows x 64 columns, 16-byte units
+      // XOR-swizzled by row) so that each warp store writes 4 full 128-byte row segments instead
+      // of 32 scattered 16-byte pieces.  Flush round rr stores row 4*rr + lane/8, unit lane%8.
+      const uint32_t stg = stage_out_base + static_cast<uint32_t>(q * 4096);
+      int64_t frow[8];
+      bool flive[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(gv[i]), p.act) * __uint_as_float(uv[i]);
-          if (live) store_row32<T>(dst_row + cc, v);
+      for (int rr = 0; rr < 8; ++rr) {
+        const int src = rr * 4 + (lane >> 3);
+        if (C::kGather) {
+          frow[rr] = ti.row_base + q * 32 + src;
+          flive[rr] = q * 32 + src < ti.valid;
+        } else {
+          frow[rr] = __shfl_sync(0xffffffffu, orow, src);
+          flive[rr] = __shfl_sync(0xffffffffu, live ? 1 : 0, src) != 0;
         }
-      } else {
+      }
+      const int unit = lane & 7;
 #pragma unroll 1
-        for (int cc = 0; cc < BN; cc += 32) {
-          uint32_t a[32];
-          tmem_ld_32x32b_x32(tb + cc, a);
-          tmem_ld_wait();
-          float v[32];
-          if (MODE == kModeG1Single) {
+      for (int cc = 0; cc < C::kOutCols; cc += 64) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(a[i]), p.act);
+        for (int h = 0; h < 2; ++h) {
+          float v[32];
+          if (MODE == kModeG1Dual) {
+            uint32_t gv[32], uv[32];
+            tmem_ld_32x32b_x32(tb + cc + 32 * h, gv);
+            tmem_ld_32x32b_x32(tb + 128 + cc + 32 * h, uv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              v[i] = act_apply(__uint_as_float(gv[i]), p.act) * __uint_as_float(uv[i]);
           } else {
+            uint32_t a[32];
+            tmem_ld_32x32b_x32(tb + cc + 32 * h, a);
+            tmem_ld_wait();
+            if (MODE == kModeG1Single) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) * wgt;
+              for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(a[i]), p.act);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) * wgt;
+            }
           }
-          if (live) store_row32<T>(dst_row + cc, v);
+          // this thread's row (lane) holds units 4h..4h+3 of the 64-column slab
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t w0 = pack2<T>(v[u * 8 + 0], v[u * 8 + 1]);
+            const uint32_t w1 = pack2<T>(v[u * 8 + 2], v[u * 8 + 3]);
+            const uint32_t w2 = pack2<T>(v[u * 8 + 4], v[u * 8 + 5]);
+            const uint32_t w3 = pack2<T>(v[u * 8 + 6], v[u * 8 + 7]);
+            const uint32_t addr = stg + lane * 128 + ((((4 * h + u) ^ (lane & 7))) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0),
+                         "r"(w1), "r"(w2), "r"(w3)
+                         : "memory");
+          }
         }
+        __syncwarp();
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int srow = rr * 4 + (lane >> 3);
+          uint4 val;
+          const uint32_t addr = stg + srow * 128 + (((unit ^ (srow & 7))) << 4);
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                       : "r"(addr)
+                       : "memory");
+          if (flive[rr])
+            *reinterpret_cast<uint4*>(out + frow[rr] * p.N + ti.n0 + cc + unit * 8) = val;
+        }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
