@@ -137,8 +137,11 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm_kernel(SimtPar
 }
 
 // out[t, :] = sum over slots j < k whose expert id is < E of slot[t*k + j, :], in slot order,
-// accumulated in f32 and rounded once.  V elements (16 bytes) per thread when H allows it.
-template <typename T, int V>
+// accumulated in f32 and rounded once.  V elements (16 bytes) per thread when H allows it.  KC
+// slots are handled per pass with all their loads in flight together (the expert ids first, then
+// every present row), so a token's k rows are fetched concurrently instead of one DRAM round trip
+// after another.
+template <typename T, int V, int KC>
 __global__ void __launch_bounds__(256) combine_slots_kernel(const T* __restrict__ slot,
                                                             const uint32_t* __restrict__ idx,
                                                             int64_t num_tokens, int k, int H,
@@ -152,26 +155,38 @@ __global__ void __launch_bounds__(256) combine_slots_kernel(const T* __restrict_
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    for (int j = 0; j < k; ++j) {
-      if (__ldg(idx + t * k + j) >= static_cast<uint32_t>(E)) continue;
-      const T* src = slot + (t * k + j) * H + c;
-      if (V * sizeof(T) == 16) {
-        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
-        const T* qe = reinterpret_cast<const T*>(&q);
+    for (int j0 = 0; j0 < k; j0 += KC) {
+      bool ok[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j)
+        ok[j] = j0 + j < k && __ldg(idx + t * k + j0 + j) < static_cast<uint32_t>(E);
+      uint4 q[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const T* src = slot + (t * k + j0 + j) * H + c;
+        if (V * sizeof(T) == 16) {
+          q[j] = ok[j] ? __ldcs(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
+        } else {
+          T* qe = reinterpret_cast<T*>(&q[j]);
+#pragma unroll
+          for (int i = 0; i < V; ++i) qe[i] = ok[j] ? src[i] : Elem<T>::from_f(0.f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        if (!ok[j]) continue;  // slot order is kept: rows are added in j order
+        const T* qe = reinterpret_cast<const T*>(&q[j]);
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(src[i]);
       }
     }
     T* dst = out + t * H + c;
     if (V * sizeof(T) == 16) {
-      uint4 q;
-      T* qe = reinterpret_cast<T*>(&q);
+      uint4 qo;
+      T* qe = reinterpret_cast<T*>(&qo);
 #pragma unroll
       for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
-      *reinterpret_cast<uint4*>(dst) = q;
+      *reinterpret_cast<uint4*>(dst) = qo;
     } else {
 #pragma unroll
       for (int i = 0; i < V; ++i) dst[i] = Elem<T>::from_f(acc[i]);
@@ -217,12 +232,20 @@ static void combine_t(const void* slot, const uint32_t* idx, int64_t T_, int k, 
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  if (vec)
-    combine_slots_kernel<T, V><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+  if (vec) {
+    if (k <= 2)
+      combine_slots_kernel<T, V, 2><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+    else if (k <= 4)
+      combine_slots_kernel<T, V, 4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+    else
+      combine_slots_kernel<T, V, 8><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+  } else {
+    combine_slots_kernel<T, 1, 4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
-  else
-    combine_slots_kernel<T, 1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        static_cast<const T*>(slot), idx, T_, k, H, E, static_cast<T*>(out));
+  }
 }
 
 int launch_combine(int dtype, const void* slot, const uint32_t* idx, int64_t num_tokens, int k,
@@ -262,7 +285,7 @@ __global__ void __launch_bounds__(256) invert_rows_kernel(const int32_t* __restr
 // out[t, :] = sum over slots j (in slot order) with inv[t*k+j] >= 0 of rows_buf[inv[t*k+j], :],
 // accumulated in f32 and rounded once -- the slot-ordered combine of combine_slots_kernel with
 // one indirection, for contributions that come back from other ranks in exchange order.
-template <typename T, int V>
+template <typename T, int V, int KC>
 __global__ void __launch_bounds__(256) combine_indirect_kernel(const T* __restrict__ rows_buf,
                                                                const int32_t* __restrict__ inv,
                                                                int64_t num_tokens, int k, int H,
@@ -276,27 +299,37 @@ __global__ void __launch_bounds__(256) combine_indirect_kernel(const T* __restri
     float acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int32_t r = __ldg(inv + t * k + j);
-      if (r < 0) continue;
-      const T* src = rows_buf + static_cast<int64_t>(r) * H + c;
-      if (V * sizeof(T) == 16) {
-        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src));
-        const T* qe = reinterpret_cast<const T*>(&q);
+    for (int j0 = 0; j0 < k; j0 += KC) {
+      int32_t r[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) r[j] = j0 + j < k ? __ldg(inv + t * k + j0 + j) : -1;
+      uint4 q[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const T* src = rows_buf + static_cast<int64_t>(r[j] < 0 ? 0 : r[j]) * H + c;
+        if (V * sizeof(T) == 16) {
+          q[j] = r[j] >= 0 ? __ldcs(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
+        } else {
+          T* qe = reinterpret_cast<T*>(&q[j]);
+#pragma unroll
+          for (int i = 0; i < V; ++i) qe[i] = r[j] >= 0 ? src[i] : Elem<T>::from_f(0.f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        if (r[j] < 0) continue;
+        const T* qe = reinterpret_cast<const T*>(&q[j]);
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(src[i]);
       }
     }
     T* dst = out + t * H + c;
     if (V * sizeof(T) == 16) {
-      uint4 q;
-      T* qe = reinterpret_cast<T*>(&q);
+      uint4 qo;
+      T* qe = reinterpret_cast<T*>(&qo);
 #pragma unroll
       for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
-      *reinterpret_cast<uint4*>(dst) = q;
+      *reinterpret_cast<uint4*>(dst) = qo;
     } else {
 #pragma unroll
       for (int i = 0; i < V; ++i) dst[i] = Elem<T>::from_f(acc[i]);
@@ -339,12 +372,20 @@ static void combine_indirect_t(const void* rows_buf, const int32_t* inv, int64_t
   constexpr int V = 16 / sizeof(T);
   const bool vec = (H % V) == 0 && (reinterpret_cast<uintptr_t>(rows_buf) % 16) == 0 &&
                    (reinterpret_cast<uintptr_t>(out) % 16) == 0;
-  if (vec)
-    combine_indirect_kernel<T, V><<<grid_for(T_ * (H / V), num_sms), 256, 0, s>>>(
+  if (vec) {
+    if (k <= 2)
+      combine_indirect_kernel<T, V, 2><<<grid_for(T_ * (H / V), num_sms), 256, 0, s>>>(
+          static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+    else if (k <= 4)
+      combine_indirect_kernel<T, V, 4><<<grid_for(T_ * (H / V), num_sms), 256, 0, s>>>(
+          static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+    else
+      combine_indirect_kernel<T, V, 8><<<grid_for(T_ * (H / V), num_sms), 256, 0, s>>>(
+          static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+  } else {
+    combine_indirect_kernel<T, 1, 4><<<grid_for(T_ * H, num_sms), 256, 0, s>>>(
         static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
-  else
-    combine_indirect_kernel<T, 1><<<grid_for(T_ * H, num_sms), 256, 0, s>>>(
-        static_cast<const T*>(rows_buf), inv, T_, k, H, static_cast<T*>(out));
+  }
 }
 
 // inv: caller scratch of num_tokens*k int32.
