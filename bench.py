@@ -184,7 +184,10 @@ def run_ours(args, world, rank, local):
     layer = None
     if ep:
         import expert_parallel
-        layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act))
+        layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act),
+                                                  mode=args.ep_mode)
+        if args.sm_reserve >= 0:
+            layer.sm_reserve = args.sm_reserve
         inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
     else:
         inp = make_inputs(cfg, seed=0, rank=rank)
@@ -313,6 +316,7 @@ def run_ours(args, world, rank, local):
         "config": {"workload": WORKLOAD_NAMES[args.config], "tokens": T, "hidden": H,
                    "intermediate": I, "experts": E, "top_k": k,
                    "parallelism": (f"ep{world}" if ep else "replicas") if world > 1 else "single-gpu",
+                   "ep_mode": args.ep_mode if ep else None,
                    "tokens_per_rank": T,
                    "l2": "inputs larger than L2 (weights 1.2 GB + activations), no flush"
                    if args.config == "c5" else "no flush"},
@@ -326,7 +330,7 @@ def run_ours(args, world, rank, local):
         line["ep_stages_ms"] = {s_: v / max(n, 1) for s_, v in st.items()}
         line["ep_rows"] = {k_: int(v) for k_, v in layer.last_stats.items()}
     if not router_only and ncalls:
-        rows = int(layer.last_stats["assignments_received"]) if ep else T * k
+        rows = layer.last_stats["assignments_received"] if ep else T * k
         n_up = 2 if moe_type == 0 else 1
         flops = {"gemm1": 2.0 * rows * H * I * n_up, "gemm2": 2.0 * rows * I * H}
         per_call = {p: phases[p] / ncalls for p in phases}
@@ -451,6 +455,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-sample", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-mode", choices=["partials", "exact"], default="partials",
+                    help="expert-parallel return: per-rank partial sums or per-slot rows")
+    ap.add_argument("--sm-reserve", type=int, default=-1,
+                    help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="override the token count (small profiling cases)")
     args = ap.parse_args()

@@ -72,12 +72,23 @@ def lib() -> ctypes.CDLL:
         L.moe_set_gemm_path.restype = I32
         L.moe_last_gemm_path.argtypes = []
         L.moe_last_gemm_path.restype = I32
+        L.moe_fused_scatter.argtypes = [P, P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, U32,
+                                         U32, P]
+        L.moe_fused_scatter.restype = ctypes.c_int
+        L.moe_ep_dest_groups.argtypes = [P, I64, I32, I32, I32, I64, P, P]
+        L.moe_ep_dest_groups.restype = ctypes.c_int
+        L.moe_ep_pack.argtypes = [P, P, P, I64, P, P, I32, I32, I32, I32, U32, P, P, P, P]
+        L.moe_ep_pack.restype = ctypes.c_int
+        L.moe_ep_entry_flat.argtypes = [P, P, P, I64, P, I32, I32, I32, P, P]
+        L.moe_ep_entry_flat.restype = ctypes.c_int
         L.moe_route_prep_ex.argtypes = [P, P, I64, I32, I32, P, P, P, P, P]
         L.moe_route_prep_ex.restype = ctypes.c_int
         L.moe_gather_rows.argtypes = [P, P, I64, I32, U32, P, P]
         L.moe_gather_rows.restype = ctypes.c_int
         L.moe_combine_rows.argtypes = [P, P, I64, I64, I32, I32, U32, P, P]
         L.moe_combine_rows.restype = ctypes.c_int
+        L.moe_set_sm_reserve.argtypes = [I32]
+        L.moe_set_sm_reserve.restype = I32
         L.moe_kernel_launches.argtypes = []
         L.moe_kernel_launches.restype = I64
         L.moe_phase_timing.argtypes = [I32]
@@ -233,6 +244,58 @@ def route_prep_ex(expert_indices: torch.Tensor, routing_weights: torch.Tensor, n
     return offsets, st_ids[:T * k], st_w[:T * k], st_f[:T * k]
 
 
+def ep_dest_groups(expert_indices: torch.Tensor, num_experts: int, num_ranks: int,
+                   tokens_per_chunk: int) -> torch.Tensor:
+    """[T, num_ranks] int32 group of each (token, rank) pair (see include/candle_moe.h)."""
+    _need_contig(expert_indices, "expert_indices")
+    T, k = expert_indices.shape
+    dev = expert_indices.device
+    groups = torch.empty((T, num_ranks), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_ep_dest_groups(_ptr(expert_indices), T, k, num_experts, num_ranks,
+                                      tokens_per_chunk, _ptr(groups), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_ep_dest_groups")
+    return groups
+
+
+def ep_pack(x: torch.Tensor, pair_token: torch.Tensor, pair_flat: torch.Tensor,
+            expert_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int,
+            num_ranks: int):
+    """(rows [U,H], meta [U, 2k] int32, slot_count [U] int32) of the U sorted pairs."""
+    U = pair_token.numel()
+    T, k = expert_indices.shape
+    H = x.shape[1]
+    dev = x.device
+    rows = torch.empty((U, H), dtype=x.dtype, device=dev)
+    meta = torch.empty((U, 2 * k), dtype=torch.int32, device=dev)
+    count = torch.empty((U,), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_ep_pack(_ptr(x), _ptr(pair_token), _ptr(pair_flat), U,
+                               _ptr(expert_indices), _ptr(routing_weights), k, num_experts,
+                               num_ranks, H, fused_moe_internal_dtype(x.dtype), _ptr(rows),
+                               _ptr(meta), _ptr(count), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_ep_pack")
+    return rows, meta, count
+
+
+def ep_entry_flat(pair_token, pair_flat, pair_start, expert_indices, num_experts, num_ranks,
+                  num_entries):
+    """[num_entries] int32: token slot t*k+j of each per-slot contribution, pair by pair."""
+    U = pair_token.numel()
+    k = expert_indices.shape[1]
+    dev = pair_token.device
+    flat = torch.empty((num_entries,), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_ep_entry_flat(_ptr(pair_token), _ptr(pair_flat), _ptr(pair_start), U,
+                                     _ptr(expert_indices), k, num_experts, num_ranks, _ptr(flat),
+                                     _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_ep_entry_flat")
+    return flat
+
+
 def gather_rows(src: torch.Tensor, index: torch.Tensor, out: Optional[torch.Tensor] = None):
     """out[r] = src[index[r]] (index int32, on the GPU)."""
     _need_contig(src, "src")
@@ -364,6 +427,30 @@ def fused_moe(input, gate_weights, up_weights, down_weights, routing_weights, ex
     return out
 
 
+def fused_moe_scatter(input, gate_weights, up_weights, down_weights, routing_weights,
+                      expert_indices, out_row, out, num_experts: int, activation: int,
+                      moe_type: int) -> torch.Tensor:
+    """Weighted contribution of every routed (t, j) written to out[out_row[t*k + j]] (no
+    combine).  out must be a [rows, H] tensor of the input's dtype."""
+    T, H = input.shape
+    I = gate_weights.shape[2]
+    k = expert_indices.shape[1]
+    dev = input.device
+    for n, t in (("input", input), ("gate_weights", gate_weights), ("up_weights", up_weights),
+                 ("routing_weights", routing_weights), ("expert_indices", expert_indices),
+                 ("out_row", out_row), ("out", out)):
+        _need_contig(t, n)
+    with torch.cuda.device(dev):
+        st = lib().moe_fused_scatter(_ptr(input), _ptr(gate_weights), _ptr(up_weights),
+                                     _ptr(down_weights), _ptr(routing_weights),
+                                     _ptr(expert_indices), _ptr(out_row), _ptr(out), T, H, I,
+                                     num_experts, k, int(activation), moe_type,
+                                     fused_moe_internal_dtype(input.dtype), _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_fused_scatter")
+    return out
+
+
 class FusedMoE:
     """src/lib.rs:244-335."""
 
@@ -416,6 +503,14 @@ def device_error_bits(device: int = 0, clear: bool = False) -> int:
 def set_gemm_path(path: int) -> int:
     """0 automatic, 1 SIMT only, 2 tensor cores only; returns the previous setting."""
     return int(lib().moe_set_gemm_path(path))
+
+
+def set_sm_reserve(sms: int) -> int:
+    """SMs the persistent GEMMs leave free for concurrent kernels; returns the previous value."""
+    prev = int(lib().moe_set_sm_reserve(sms))
+    if prev < 0:
+        raise ValueError(f"sm reserve {sms} out of range")
+    return prev
 
 
 def last_gemm_path() -> int:

@@ -28,6 +28,7 @@ namespace {
 thread_local int t_last_status = MOE_OK;
 thread_local int t_last_path = 0;
 std::atomic<int> g_gemm_path{0};
+std::atomic<int> g_sm_reserve{0};  // SMs the persistent GEMMs leave free (moe_set_sm_reserve)
 
 constexpr int kMaxDevices = 64;
 
@@ -139,8 +140,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Workspace of one fused call (byte offsets into one buffer).
 struct FusedLayout {
-  size_t offsets, tile_prefix, sorted_token, sorted_flat, sorted_w, prep_scratch, inter, slot,
-      total;
+  size_t offsets, tile_prefix, counters, sorted_token, sorted_flat, sorted_w, prep_scratch, inter,
+      slot, total;
 };
 
 FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype) {
@@ -150,6 +151,7 @@ FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype) {
   size_t o = 0;
   L.offsets = o;        o += align256(sizeof(int32_t) * (E + 2));
   L.tile_prefix = o;    o += align256(sizeof(int32_t) * (E + 1));
+  L.counters = o;       o += align256(sizeof(uint32_t) * 2);  // tile counters of the 2 GEMMs
   L.sorted_token = o;   o += align256(sizeof(int32_t) * rows);
   L.sorted_flat = o;    o += align256(sizeof(int32_t) * rows);
   L.sorted_w = o;       o += align256(sizeof(float) * rows);
@@ -178,10 +180,13 @@ bool sm100_shape_ok(int dtype, const void* x, const void* g, const void* u, cons
   return true;
 }
 
+// out_row == nullptr: the drop-in semantics (output [T,H], the k slots of a token combined).
+// out_row != nullptr: no combine; the weighted contribution of every routed (t, j) is written to
+// row out_row[t*k + j] of `output` (rows must be distinct).
 int fused_impl(const void* input, const void* gate, const void* up, const void* down,
                const float* rw, const uint32_t* idx, void* output, int64_t T, int H, int I, int E,
                int k, int act, uint32_t moe_type, uint32_t dtype, void* workspace,
-               size_t workspace_bytes, cudaStream_t stream) {
+               size_t workspace_bytes, cudaStream_t stream, const int32_t* out_row = nullptr) {
   t_last_path = 0;
   if (dtype > 2 || moe_type > 1) return MOE_ERR_INVALID_ARG;
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return MOE_ERR_INVALID_ARG;
@@ -203,7 +208,10 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   if (gpath == 2 && !use_sm100) return MOE_ERR_UNSUPPORTED;
   const int bm = use_sm100 ? sm100_tile_m() : simt_tile_m();
 
-  const FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype));
+  const bool scatter = out_row != nullptr;
+  // scatter writes each contribution to its own output row: no slot buffer, no combine
+  FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype));
+  if (scatter) L.total = L.slot;
   char* ws = static_cast<char*>(workspace);
   bool owned = false;
   if (ws == nullptr) {
@@ -225,7 +233,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   float* s_w = reinterpret_cast<float*>(ws + L.sorted_w);
   void* prep_scratch = ws + L.prep_scratch;
   void* inter = ws + L.inter;
-  void* slot = (k > 1) ? static_cast<void*>(ws + L.slot) : output;
+  void* slot = (k > 1 && !scatter) ? static_cast<void*>(ws + L.slot) : output;
 
   const int64_t rows = T * k;
   const int64_t mtile_bound = rows / bm + (E < rows ? E : rows);
@@ -238,11 +246,14 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
                          prep_scratch, stream) == 0
            ? MOE_OK
            : MOE_ERR_UNSUPPORTED;
-  if (st == MOE_OK && k == 1)
+  if (st == MOE_OK && k == 1 && !scatter)
     if (cudaMemsetAsync(output, 0, elt * static_cast<size_t>(T) * H, stream) != cudaSuccess)
       st = MOE_ERR_CUDA;
   if (ev) cudaEventRecord(ev[1], stream);
 
+  uint32_t* counters = reinterpret_cast<uint32_t*>(ws + L.counters);
+  if (st == MOE_OK && use_sm100)
+    if (cudaMemsetAsync(counters, 0, 2 * sizeof(uint32_t), stream) != cudaSuccess) st = MOE_ERR_CUDA;
   if (st == MOE_OK && use_sm100) {
     // GEMM-1
     CUtensorMap mA, mB0, mB1;
@@ -254,6 +265,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
               make_map_2d(&mB0, dtype, gate, I, static_cast<uint64_t>(E) * H, 64, 64) &&
               make_map_2d(&mB1, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 64);
     Sm100Params p;
+    p.out_row = nullptr;
     p.a_rows = input;
     p.offsets = offsets;
     p.tile_prefix = tile_prefix;
@@ -265,11 +277,13 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     p.err = ds->err_word;
     if (ok) {
       p.out = inter;
+      p.tile_counter = counters;
       p.N = I;
       p.K = H;
       p.n_tiles = I / cols1;
       const int64_t tiles = mtile_bound * p.n_tiles;
-      const int grid = static_cast<int>(tiles < ds->num_sms ? tiles : ds->num_sms);
+      const int sms = ds->num_sms - g_sm_reserve.load();
+      const int grid = static_cast<int>(tiles < sms ? tiles : sms);
       if (launch_sm100_gemm(static_cast<int>(dtype), mode1, bn1, mA, mB0, mB1, p, grid, stream))
         ok = false;
     }
@@ -286,11 +300,14 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     }
     if (ok) {
       p.out = slot;
+      p.out_row = out_row;
+      p.tile_counter = counters + 1;
       p.N = H;
       p.K = I;
       p.n_tiles = H / sm100_out_cols(mode2, bn2);
       const int64_t tiles = mtile_bound * p.n_tiles;
-      const int grid = static_cast<int>(tiles < ds->num_sms ? tiles : ds->num_sms);
+      const int sms = ds->num_sms - g_sm_reserve.load();
+      const int grid = static_cast<int>(tiles < sms ? tiles : sms);
       if (launch_sm100_gemm(static_cast<int>(dtype), mode2, bn2, mA, mB0, mB0, p, grid, stream))
         ok = false;
     }
@@ -298,6 +315,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     t_last_path = 2;
   } else if (st == MOE_OK) {
     SimtParams p;
+    p.out_row = nullptr;
     p.offsets = offsets;
     p.tile_prefix = tile_prefix;
     p.sorted_token = s_token;
@@ -320,6 +338,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.b0 = moe_type == 0 ? down : up;
       p.b1 = nullptr;
       p.out = slot;
+      p.out_row = out_row;
       p.N = H;
       p.K = I;
       st = launch_simt_gemm(static_cast<int>(dtype), moe_type == 0 ? 2 : 3, p, mtile_bound, stream) == 0
@@ -330,7 +349,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   }
   if (ev) cudaEventRecord(ev[3], stream);
   launches += 2;
-  if (st == MOE_OK && k > 1) {
+  if (st == MOE_OK && k > 1 && !scatter) {
     launch_combine(static_cast<int>(dtype), slot, idx, T, k, H, E, output, ds->num_sms, stream);
     ++launches;
   }
@@ -491,6 +510,67 @@ CMOE_API int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, 
   return finish(st);
 }
 
+CMOE_API int moe_ep_dest_groups(const uint32_t* expert_indices, int64_t num_tokens, int32_t topk,
+                                int32_t num_experts, int32_t num_ranks,
+                                int64_t tokens_per_chunk, int32_t* groups, void* stream) {
+  if (num_tokens < 0 || topk <= 0 || num_experts <= 0 || num_ranks <= 0 || tokens_per_chunk <= 0)
+    return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MOE_OK;
+  if (!expert_indices || !groups) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_ep_dest_groups(expert_indices, num_tokens, topk, num_experts, num_ranks,
+                            tokens_per_chunk, groups, ds->num_sms,
+                            static_cast<cudaStream_t>(stream)))
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_ep_pack(const void* input, const int32_t* pair_token, const int32_t* pair_flat,
+                         int64_t num_pairs, const uint32_t* expert_indices,
+                         const float* routing_weights, int32_t topk, int32_t num_experts,
+                         int32_t num_ranks, int32_t hidden_dim, uint32_t dtype, void* rows,
+                         int32_t* meta, int32_t* slot_count, void* stream) {
+  if (num_pairs < 0 || topk <= 0 || num_experts <= 0 || num_ranks <= 0 || hidden_dim <= 0 ||
+      dtype > 2)
+    return MOE_ERR_INVALID_ARG;
+  if (num_pairs == 0) return MOE_OK;
+  if (!input || !pair_token || !pair_flat || !expert_indices || !routing_weights || !rows ||
+      !meta || !slot_count)
+    return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_ep_pack(static_cast<int>(dtype), input, pair_token, pair_flat, num_pairs,
+                     expert_indices, routing_weights, topk, num_experts, num_ranks, hidden_dim,
+                     rows, meta, slot_count, ds->num_sms, static_cast<cudaStream_t>(stream)))
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
+                               const int64_t* pair_start, int64_t num_pairs,
+                               const uint32_t* expert_indices, int32_t topk, int32_t num_experts,
+                               int32_t num_ranks, int32_t* flat, void* stream) {
+  if (num_pairs < 0 || topk <= 0 || num_experts <= 0 || num_ranks <= 0)
+    return MOE_ERR_INVALID_ARG;
+  if (num_pairs == 0) return MOE_OK;
+  if (!pair_token || !pair_flat || !pair_start || !expert_indices || !flat)
+    return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_ep_entry_flat(pair_token, pair_flat, pair_start, num_pairs, expert_indices, topk,
+                           num_experts, num_ranks, flat, ds->num_sms,
+                           static_cast<cudaStream_t>(stream)))
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
 CMOE_API size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim,
                                          int32_t intermediate_dim, int32_t num_experts,
                                          int32_t topk, uint32_t moe_type, uint32_t dtype) {
@@ -514,6 +594,20 @@ CMOE_API int moe_fused_v2(const void* input, const void* gate_weights, const voi
                     expert_indices, output, num_tokens, hidden_dim, intermediate_dim,
                     num_experts, topk, activation_type, moe_type, dtype, workspace,
                     workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+CMOE_API int moe_fused_scatter(const void* input, const void* gate_weights,
+                               const void* up_weights, const void* down_weights,
+                               const float* routing_weights, const uint32_t* expert_indices,
+                               const int32_t* out_row, void* output, int64_t num_tokens,
+                               int32_t hidden_dim, int32_t intermediate_dim, int32_t num_experts,
+                               int32_t topk, int32_t activation_type, uint32_t moe_type,
+                               uint32_t dtype, void* stream) {
+  if (!out_row) return MOE_ERR_INVALID_ARG;
+  return fused_impl(input, gate_weights, up_weights, down_weights, routing_weights,
+                    expert_indices, output, num_tokens, hidden_dim, intermediate_dim,
+                    num_experts, topk, activation_type, moe_type, dtype, nullptr, 0,
+                    static_cast<cudaStream_t>(stream), out_row);
 }
 
 CMOE_API void fused_moe(void* input, void* gate_weights, void* up_weights, void* down_weights,
@@ -549,6 +643,11 @@ CMOE_API int32_t moe_set_gemm_path(int32_t path) {
 }
 
 CMOE_API int32_t moe_last_gemm_path(void) { return t_last_path; }
+
+CMOE_API int32_t moe_set_sm_reserve(int32_t sms) {
+  if (sms < 0 || sms > 128) return -1;
+  return g_sm_reserve.exchange(sms);
+}
 
 CMOE_API int64_t moe_kernel_launches(void) { return g_launches.load(); }
 

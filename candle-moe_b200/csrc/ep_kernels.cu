@@ -1,0 +1,131 @@
+// Bookkeeping kernels of the expert-parallel exchange (candle-moe_b200/expert_parallel.py).
+//
+// The reference has no multi-GPU path.  With G ranks owning E/G experts each, a token is sent
+// once to every rank that owns at least one of its k experts.  These kernels turn the router's
+// [T,k] expert ids into (token, rank) pairs, pack the pairs' rows and slot metadata for the
+// all-to-all, and map the contributions that come back to the token slots they belong to.
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cmoe {
+
+// groups[t*G + d] = (t / tokens_per_chunk) * G + d when token t has an expert on rank d, else
+// chunks*G (ignored by route preparation).  Ids >= E (skipped everywhere) select no rank.
+__global__ void __launch_bounds__(256) ep_dest_groups_kernel(const uint32_t* __restrict__ idx,
+                                                             int64_t T, int k, int E, int El,
+                                                             int G, int64_t tokens_per_chunk,
+                                                             int32_t* __restrict__ groups) {
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < T;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint32_t mask = 0;  // G <= 32
+    for (int j = 0; j < k; ++j) {
+      const uint32_t e = __ldg(idx + t * k + j);
+      if (e < static_cast<uint32_t>(E)) mask |= 1u << (e / El);
+    }
+    const int32_t chunk = static_cast<int32_t>(t / tokens_per_chunk);
+    const int32_t chunks_g = static_cast<int32_t>(((T + tokens_per_chunk - 1) / tokens_per_chunk) * G);
+    for (int d = 0; d < G; ++d)
+      groups[t * G + d] = (mask >> d) & 1u ? chunk * G + d : chunks_g;
+  }
+}
+
+// For the U sorted (token, rank) pairs (pair_token[r], pair_flat[r] = t*G + d): copy x[t] to
+// rows[r] (one warp per pair, 16-byte lanes) and write the pair's slot metadata: meta[r*2k + j] =
+// local expert id of slot j if that slot's expert lives on rank d, else El; meta[r*2k + k + j] =
+// the slot's routing weight bits (0 for foreign slots).  count[r] = slots of the pair.
+template <typename V>
+__global__ void __launch_bounds__(256) ep_pack_kernel(
+    const V* __restrict__ x, const int32_t* __restrict__ pair_token,
+    const int32_t* __restrict__ pair_flat, int64_t U, const uint32_t* __restrict__ idx,
+    const float* __restrict__ w, int k, int E, int El, int G, int vec_per_row,
+    V* __restrict__ rows, int32_t* __restrict__ meta, int32_t* __restrict__ count) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < U; r += nwarps) {
+    const int64_t t = __ldg(pair_token + r);
+    const int d = __ldg(pair_flat + r) % G;
+    const V* src = x + t * vec_per_row;
+    V* dst = rows + r * vec_per_row;
+    for (int c = lane; c < vec_per_row; c += 32) dst[c] = __ldg(src + c);
+    if (lane < k) {
+      const uint32_t e = __ldg(idx + t * k + lane);
+      const bool mine = e < static_cast<uint32_t>(E) && static_cast<int>(e / El) == d;
+      meta[r * 2 * k + lane] = mine ? static_cast<int32_t>(e % El) : El;
+      meta[r * 2 * k + k + lane] = mine ? __float_as_int(__ldg(w + t * k + lane)) : 0;
+      const uint32_t ballot = __ballot_sync(0xffffffffu >> (32 - k), mine);
+      if (lane == 0) count[r] = __popc(ballot);
+    }
+  }
+}
+
+// Exact mode: the contributions of pair r come back as count[r] consecutive rows starting at
+// start[r] (exclusive prefix of count), one per slot of the pair in slot order; record the token
+// slot each row belongs to: flat[start[r] + i] = t*k + j for the pair's i-th slot j.
+__global__ void __launch_bounds__(256) ep_entry_flat_kernel(
+    const int32_t* __restrict__ pair_token, const int32_t* __restrict__ pair_flat,
+    const int64_t* __restrict__ start, int64_t U, const uint32_t* __restrict__ idx, int k, int E,
+    int El, int G, int32_t* __restrict__ flat) {
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < U;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = __ldg(pair_token + r);
+    const int d = __ldg(pair_flat + r) % G;
+    int64_t pos = __ldg(start + r);
+    for (int j = 0; j < k; ++j) {
+      const uint32_t e = __ldg(idx + t * k + j);
+      if (e < static_cast<uint32_t>(E) && static_cast<int>(e / El) == d)
+        flat[pos++] = static_cast<int32_t>(t * k + j);
+    }
+  }
+}
+
+static unsigned ep_grid(int64_t work, int num_sms) {
+  int64_t b = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return static_cast<unsigned>(b);
+}
+
+int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,
+                          int64_t tokens_per_chunk, int32_t* groups, int num_sms,
+                          cudaStream_t s) {
+  if (G < 1 || G > 32 || E % G != 0 || tokens_per_chunk < 1) return 1;
+  if (T <= 0) return 0;
+  ep_dest_groups_kernel<<<ep_grid(T, num_sms), 256, 0, s>>>(idx, T, k, E, E / G, G,
+                                                            tokens_per_chunk, groups);
+  return 0;
+}
+
+int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const int32_t* pair_flat,
+                   int64_t U, const uint32_t* idx, const float* w, int k, int E, int G, int H,
+                   void* rows, int32_t* meta, int32_t* count, int num_sms, cudaStream_t s) {
+  if (G < 1 || G > 32 || E % G != 0 || k > 32) return 1;
+  if (U <= 0) return 0;
+  const size_t row_bytes = static_cast<size_t>(H) * (dtype == kF32 ? 4 : 2);
+  const unsigned grid = ep_grid(U * 32, num_sms);
+  if (row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(rows) % 16 == 0)
+    ep_pack_kernel<uint4><<<grid, 256, 0, s>>>(
+        static_cast<const uint4*>(x), pair_token, pair_flat, U, idx, w, k, E, E / G, G,
+        static_cast<int>(row_bytes / 16), static_cast<uint4*>(rows), meta, count);
+  else
+    ep_pack_kernel<uint16_t><<<grid, 256, 0, s>>>(
+        static_cast<const uint16_t*>(x), pair_token, pair_flat, U, idx, w, k, E, E / G, G,
+        static_cast<int>(row_bytes / 2), static_cast<uint16_t*>(rows), meta, count);
+  return 0;
+}
+
+int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
+                         const int64_t* start, int64_t U, const uint32_t* idx, int k, int E,
+                         int G, int32_t* flat, int num_sms, cudaStream_t s) {
+  if (G < 1 || G > 32 || E % G != 0) return 1;
+  if (U <= 0) return 0;
+  ep_entry_flat_kernel<<<ep_grid(U, num_sms), 256, 0, s>>>(pair_token, pair_flat, start, U, idx,
+                                                           k, E, E / G, G, flat);
+  return 0;
+}
+
+}  // namespace cmoe

@@ -31,6 +31,7 @@ struct SimtParams {
   const int32_t* sorted_flat;   // [rows]
   const float* sorted_w;        // [rows]
   void* out;                    // GEMM-1: intermediate [rows, N]; GEMM-2: slot [T*k, N] / out [T, N]
+  const int32_t* out_row;       // GEMM-2 only: output row of flat index t*k+j (null: the flat index)
   int N, K, E, act;
 };
 int simt_tile_m();
@@ -61,11 +62,13 @@ struct Sm100Params {
   const int32_t* sorted_flat;   // [rows]
   const float* sorted_w;        // [rows]
   void* out;                    // GEMM-1: intermediate [rows, N]; GEMM-2: slot [T*k, N] / out [T, N]
+  const int32_t* out_row;       // GEMM-2 only: output row of flat index t*k+j (null: the flat index)
   int N;                        // output columns (I for GEMM-1, H for GEMM-2)
   int K;                        // reduction length (H for GEMM-1, I for GEMM-2)
   int E;
   int act;
   int n_tiles;                  // N / output columns per tile
+  uint32_t* tile_counter;       // zeroed before the launch: next unclaimed tile
   uint32_t* err;                // device error word
 };
 int sm100_tile_m();
@@ -77,5 +80,16 @@ bool sm100_set_attributes();
 int sm100_out_cols(int mode, int bn);
 int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
+
+// ---- ep_kernels.cu -------------------------------------------------------------------------
+int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,
+                          int64_t tokens_per_chunk, int32_t* groups, int num_sms,
+                          cudaStream_t s);
+int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const int32_t* pair_flat,
+                   int64_t U, const uint32_t* idx, const float* w, int k, int E, int G, int H,
+                   void* rows, int32_t* meta, int32_t* count, int num_sms, cudaStream_t s);
+int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
+                         const int64_t* start, int64_t U, const uint32_t* idx, int k, int E,
+                         int G, int32_t* flat, int num_sms, cudaStream_t s);
 
 }  // namespace cmoe

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm_kernel(SimtPar
       orow = row_base + r;
     } else {
       orow = __ldg(p.sorted_flat + row_base + r);
+      if (p.out_row) orow = __ldg(p.out_row + orow);
       wgt = __ldg(p.sorted_w + row_base + r);
     }
 #pragma unroll

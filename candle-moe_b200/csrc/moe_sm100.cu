@@ -41,6 +41,7 @@ constexpr int kTmemCols = 512;
 constexpr int kAccStride = 256;                                  // TMEM columns per buffer
 constexpr int kSm100Threads = 256;
 constexpr int kGatherThreads = 64;                               // warps 2-3 gather A rows
+constexpr int kTileRing = 4;                                     // tile ids published ahead
 constexpr int kStageOutBytes = 4 * 4096;                         // epilogue staging, 4 KB/warp
 // stages + alignment slack + epilogue staging; the tile tables (2E+3 ints) follow
 constexpr size_t kSm100SmemBase =
@@ -84,6 +85,22 @@ __device__ __forceinline__ TileInfo decode_tile(const int32_t* s_tp, const int32
   return ti;
 }
 
+// Next tile id from the scheduler ring (-1: no more tiles, -2: gave up waiting).  Every lane of
+// the calling warp gets the id; lane 0 releases the slot.
+__device__ __forceinline__ int next_tile_from_ring(uint64_t* tfull, uint64_t* tempty,
+                                                   const int* ring, int it, volatile int* abort,
+                                                   uint32_t* err, bool whole_warp) {
+  const int slot = it % kTileRing;
+  const uint32_t par = static_cast<uint32_t>((it / kTileRing) & 1);
+  bool got = mbar_wait_bounded(smem_addr(&tfull[slot]), par, abort, err, kErrWaitFull);
+  if (whole_warp) got = __all_sync(0xffffffffu, got);
+  if (!got) return -2;
+  const int t = ring[slot];
+  if (whole_warp) __syncwarp();
+  if (!whole_warp || (threadIdx.x & 31) == 0) mbar_arrive(smem_addr(&tempty[slot]));
+  return t;
+}
+
 template <typename T>
 __device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -109,6 +126,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   __shared__ __align__(8) uint64_t bar_empty[kStages];
   __shared__ __align__(8) uint64_t bar_accf[2];
   __shared__ __align__(8) uint64_t bar_acce[2];
+  __shared__ __align__(8) uint64_t bar_tfull[kTileRing];   // tile id published
+  __shared__ __align__(8) uint64_t bar_tempty[kTileRing];  // tile id read by every consumer
+  __shared__ int s_tile[kTileRing];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
 
@@ -138,6 +158,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       mbar_init(smem_addr(&bar_accf[b]), 1);
       mbar_init(smem_addr(&bar_acce[b]), 4);
     }
+    // consumers of a tile id: the MMA thread, 4 epilogue warps, and the 2 gather warps
+    for (int i = 0; i < kTileRing; ++i) {
+      mbar_init(smem_addr(&bar_tfull[i]), 1);
+      mbar_init(smem_addr(&bar_tempty[i]), 5 + (C::kGather ? 2 : 0));
+    }
     s_abort = 0;
     fence_barrier_init();
   }
@@ -159,10 +184,24 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (B; A too
     // when A is a contiguous run of sorted rows)
+    // Also the tile scheduler: tiles are taken from a global counter (so CTAs that start late
+    // take fewer), and each tile id is published to the other roles through a 4-deep ring.
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      int tile = static_cast<int>(atomicAdd(p.tile_counter, 1u));
+      for (int it = 0; ok; ++it) {
+        const int slot = it % kTileRing;
+        if (!mbar_wait_bounded(smem_addr(&bar_tempty[slot]),
+                               static_cast<uint32_t>((it / kTileRing) & 1) ^ 1u, &s_abort, p.err,
+                               kErrWaitEmpty)) {
+          break;
+        }
+        if (tile >= total_tiles) tile = -1;
+        s_tile[slot] = tile;
+        mbar_arrive(smem_addr(&bar_tfull[slot]));
+        if (tile < 0) break;
+        const int next_tile = static_cast<int>(atomicAdd(p.tile_counter, 1u));
         const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
@@ -195,6 +234,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             phase ^= 1u;
           }
         }
+        tile = next_tile;
       }
     }
   } else if (warp == 1) {
@@ -204,8 +244,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           umma_idesc(UmmaFmt<T>::v, MODE == kModeG2K ? 0u : 1u, kBM, C::kMmaN);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int lt = 0;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++lt) {
+      for (int lt = 0; ok; ++lt) {
+        const int tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, lt, &s_abort, p.err,
+                                             false);
+        if (tile < 0) break;
         const int buf = lt & 1;
         const uint32_t par = static_cast<uint32_t>((lt >> 1) & 1) ^ 1u;
         if (!mbar_wait_bounded(smem_addr(&bar_acce[buf]), par, &s_abort, p.err, kErrWaitAccEmpty)) {
@@ -257,7 +299,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       const T* x = static_cast<const T*>(p.a_rows);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int it = 0; ok; ++it) {
+        const int tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, it, &s_abort, p.err,
+                                             true);
+        if (tile < 0) break;
         const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
         const T* src[16];
         const int last = ti.valid - 1;
@@ -291,8 +336,10 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     const int q = warp - 4;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
     T* out = static_cast<T*>(p.out);
-    int lt = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++lt) {
+    for (int lt = 0;; ++lt) {
+      const int tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, lt, &s_abort, p.err,
+                                           true);
+      if (tile < 0) break;
       const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
       const int buf = lt & 1;
       const bool live = r < ti.valid;
@@ -302,6 +349,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
         orow = ti.row_base + r;
       } else if (live) {
         orow = __ldg(p.sorted_flat + ti.row_base + r);
+        if (p.out_row) orow = __ldg(p.out_row + orow);
         wgt = __ldg(p.sorted_w + ti.row_base + r);
       }
       bool got = mbar_wait_bounded(smem_addr(&bar_accf[buf]), static_cast<uint32_t>((lt >> 1) & 1),

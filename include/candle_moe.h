@@ -131,6 +131,34 @@ int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, int64_t r
                      int64_t num_tokens, int32_t topk, int32_t hidden_dim, uint32_t dtype,
                      void* output, void* stream);
 
+/*
+ * Expert-parallel bookkeeping (no counterpart in the reference, which has no multi-GPU path).
+ * With num_ranks ranks owning num_experts/num_ranks experts each:
+ *
+ * moe_ep_dest_groups: groups[t*num_ranks + d] = (t / tokens_per_chunk) * num_ranks + d when
+ *   token t has one of its topk experts on rank d, else (number of chunks) * num_ranks; route
+ *   preparation over these groups buckets the (token, rank) pairs to send.
+ * moe_ep_pack: for the num_pairs sorted pairs (pair_token[r] = t, pair_flat[r] = t*num_ranks + d)
+ *   copy input row t to rows[r], write the pair's topk-slot metadata (meta[r*2*topk + j] = local
+ *   expert id of slot j if its expert lives on rank d, else num_experts/num_ranks;
+ *   meta[r*2*topk + topk + j] = that slot's routing weight bits, or 0) and slot_count[r] = the
+ *   pair's slots.
+ * moe_ep_entry_flat: with pair_start the exclusive prefix of slot_count, write
+ *   flat[pair_start[r] + i] = t*topk + j for the pair's i-th slot j (the token slot of each
+ *   per-slot contribution returned for pair r).
+ */
+int moe_ep_dest_groups(const uint32_t* expert_indices, int64_t num_tokens, int32_t topk,
+                       int32_t num_experts, int32_t num_ranks, int64_t tokens_per_chunk,
+                       int32_t* groups, void* stream);
+int moe_ep_pack(const void* input, const int32_t* pair_token, const int32_t* pair_flat,
+                int64_t num_pairs, const uint32_t* expert_indices, const float* routing_weights,
+                int32_t topk, int32_t num_experts, int32_t num_ranks, int32_t hidden_dim,
+                uint32_t dtype, void* rows, int32_t* meta, int32_t* slot_count, void* stream);
+int moe_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
+                      const int64_t* pair_start, int64_t num_pairs,
+                      const uint32_t* expert_indices, int32_t topk, int32_t num_experts,
+                      int32_t num_ranks, int32_t* flat, void* stream);
+
 /* Bytes of caller workspace that moe_fused_v2 needs for these sizes (0 for num_tokens == 0). */
 size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim, int32_t intermediate_dim,
                                 int32_t num_experts, int32_t topk, uint32_t moe_type,
@@ -150,6 +178,21 @@ int moe_fused_v2(const void* input, const void* gate_weights, const void* up_wei
                  size_t workspace_bytes, void* stream);
 
 /*
+ * The expert computation of fused_moe without the combine: the weighted contribution
+ * w[t,j] * y_{e(t,j)}(x_t) of every routed (t, j) (ids >= num_experts skipped) is written,
+ * rounded to `dtype`, to row out_row[t*topk + j] of `output` ([rows, hidden_dim]; the rows of
+ * routed slots must be distinct; other rows are left untouched).  This is the remote half of the
+ * expert-parallel layer, which writes contributions straight into the buffer it sends back (no
+ * counterpart in the reference, which has no multi-GPU path).
+ */
+int moe_fused_scatter(const void* input, const void* gate_weights, const void* up_weights,
+                      const void* down_weights, const float* routing_weights,
+                      const uint32_t* expert_indices, const int32_t* out_row, void* output,
+                      int64_t num_tokens, int32_t hidden_dim, int32_t intermediate_dim,
+                      int32_t num_experts, int32_t topk, int32_t activation_type,
+                      uint32_t moe_type, uint32_t dtype, void* stream);
+
+/*
  * Error bits the tensor-core kernels raised on `device` (a bounded wait that ran out; see
  * DevErr in csrc/common.cuh).  Synchronises the device.  clear != 0 resets them.
  */
@@ -161,6 +204,13 @@ uint32_t moe_device_error_bits(int32_t device, int32_t clear);
  * return MOE_ERR_UNSUPPORTED).  Process-wide; returns the previous value.
  */
 int32_t moe_set_gemm_path(int32_t path);
+
+/*
+ * Number of SMs the persistent tensor-core GEMMs leave unused (0 by default, at most 128), so
+ * that kernels running concurrently on other streams -- the collectives of the expert-parallel
+ * exchange -- keep SMs of their own.  Process-wide; returns the previous value.
+ */
+int32_t moe_set_sm_reserve(int32_t sms);
 
 /* Which family served the last moe_fused_v2 / fused_moe call of this thread: 1 SIMT, 2 tensor
  * cores, 0 none. */
