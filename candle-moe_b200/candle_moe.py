@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
         L.moe_ep_pack.restype = ctypes.c_int
         L.moe_ep_entry_flat.argtypes = [P, P, P, I64, P, I32, I32, I32, P, P]
         L.moe_ep_entry_flat.restype = ctypes.c_int
+        L.moe_segment_sum_rows.argtypes = [P, P, I64, I32, U32, P, P]
+        L.moe_segment_sum_rows.restype = ctypes.c_int
         L.moe_route_prep_ex.argtypes = [P, P, I64, I32, I32, P, P, P, P, P]
         L.moe_route_prep_ex.restype = ctypes.c_int
         L.moe_gather_rows.argtypes = [P, P, I64, I32, U32, P, P]
@@ -294,6 +296,23 @@ def ep_entry_flat(pair_token, pair_flat, pair_start, expert_indices, num_experts
     if st != MOE_OK:
         raise MoeError(st, "moe_ep_entry_flat")
     return flat
+
+
+def segment_sum_rows(rows_in: torch.Tensor, segment_start: torch.Tensor) -> torch.Tensor:
+    """out[r] = sum(rows_in[segment_start[r]:segment_start[r+1]]) (f32 accumulation)."""
+    _need_contig(rows_in, "rows_in")
+    _need_contig(segment_start, "segment_start")
+    R = segment_start.numel() - 1
+    H = rows_in.shape[1]
+    dev = rows_in.device
+    out = torch.empty((R, H), dtype=rows_in.dtype, device=dev)
+    with torch.cuda.device(dev):
+        st = lib().moe_segment_sum_rows(_ptr(rows_in), _ptr(segment_start), R, H,
+                                        fused_moe_internal_dtype(rows_in.dtype), _ptr(out),
+                                        _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_segment_sum_rows")
+    return out
 
 
 def gather_rows(src: torch.Tensor, index: torch.Tensor, out: Optional[torch.Tensor] = None):

@@ -571,6 +571,21 @@ CMOE_API int moe_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_fl
   return finish(MOE_OK);
 }
 
+CMOE_API int moe_segment_sum_rows(const void* rows_in, const int64_t* segment_start,
+                                 int64_t num_segments, int32_t hidden_dim, uint32_t dtype,
+                                 void* output, void* stream) {
+  if (num_segments < 0 || hidden_dim <= 0 || dtype > 2) return MOE_ERR_INVALID_ARG;
+  if (num_segments == 0) return MOE_OK;
+  if (!rows_in || !segment_start || !output) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  launch_segment_sum_rows(static_cast<int>(dtype), rows_in, segment_start, num_segments,
+                          hidden_dim, output, ds->num_sms, static_cast<cudaStream_t>(stream));
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
 CMOE_API size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim,
                                          int32_t intermediate_dim, int32_t num_experts,
                                          int32_t topk, uint32_t moe_type, uint32_t dtype) {

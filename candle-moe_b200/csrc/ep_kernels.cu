@@ -81,6 +81,59 @@ __global__ void __launch_bounds__(256) ep_entry_flat_kernel(
   }
 }
 
+// out[r, :] = sum of rows_in[start[r] .. start[r+1]) in order, f32 accumulation, one rounding:
+// the per-rank partial of a (token, rank) pair from its slot contributions, which the scatter
+// GEMM wrote consecutively in slot order.  Up to KC rows of a segment are loaded at once.
+template <typename T, int V, int KC>
+__global__ void __launch_bounds__(256) segment_sum_rows_kernel(const T* __restrict__ rows_in,
+                                                               const int64_t* __restrict__ start,
+                                                               int64_t R, int H,
+                                                               T* __restrict__ out) {
+  const int vec_per_row = H / V;
+  const int64_t total = R * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = v / vec_per_row;
+    const int c = static_cast<int>(v - r * vec_per_row) * V;
+    const int64_t s0 = __ldg(start + r), s1 = __ldg(start + r + 1);
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int64_t b = s0; b < s1; b += KC) {
+      uint4 q[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const T* src = rows_in + (b + j < s1 ? b + j : s0) * H + c;
+        if (V * sizeof(T) == 16) {
+          q[j] = b + j < s1 ? __ldcs(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
+        } else {
+          T* qe = reinterpret_cast<T*>(&q[j]);
+#pragma unroll
+          for (int i = 0; i < V; ++i) qe[i] = b + j < s1 ? src[i] : Elem<T>::from_f(0.f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        if (b + j >= s1) continue;
+        const T* qe = reinterpret_cast<const T*>(&q[j]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
+      }
+    }
+    T* dst = out + r * H + c;
+    if (V * sizeof(T) == 16) {
+      uint4 qo;
+      T* qe = reinterpret_cast<T*>(&qo);
+#pragma unroll
+      for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
+      *reinterpret_cast<uint4*>(dst) = qo;
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) dst[i] = Elem<T>::from_f(acc[i]);
+    }
+  }
+}
+
 static unsigned ep_grid(int64_t work, int num_sms) {
   int64_t b = (work + 255) / 256;
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
@@ -125,6 +178,29 @@ int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
   if (U <= 0) return 0;
   ep_entry_flat_kernel<<<ep_grid(U, num_sms), 256, 0, s>>>(pair_token, pair_flat, start, U, idx,
                                                            k, E, E / G, G, flat);
+  return 0;
+}
+
+template <typename T>
+static void segment_sum_t(const void* in, const int64_t* start, int64_t R, int H, void* out,
+                          int num_sms, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = (H % V) == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (vec)
+    segment_sum_rows_kernel<T, V, 8><<<ep_grid(R * (H / V), num_sms), 256, 0, s>>>(
+        static_cast<const T*>(in), start, R, H, static_cast<T*>(out));
+  else
+    segment_sum_rows_kernel<T, 1, 4><<<ep_grid(R * H, num_sms), 256, 0, s>>>(
+        static_cast<const T*>(in), start, R, H, static_cast<T*>(out));
+}
+
+int launch_segment_sum_rows(int dtype, const void* in, const int64_t* start, int64_t R, int H,
+                            void* out, int num_sms, cudaStream_t s) {
+  if (R <= 0) return 0;
+  if (dtype == kF32) segment_sum_t<float>(in, start, R, H, out, num_sms, s);
+  else if (dtype == kBF16) segment_sum_t<__nv_bfloat16>(in, start, R, H, out, num_sms, s);
+  else segment_sum_t<__half>(in, start, R, H, out, num_sms, s);
   return 0;
 }
 

@@ -88,6 +88,8 @@ int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,
 int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const int32_t* pair_flat,
                    int64_t U, const uint32_t* idx, const float* w, int k, int E, int G, int H,
                    void* rows, int32_t* meta, int32_t* count, int num_sms, cudaStream_t s);
+int launch_segment_sum_rows(int dtype, const void* in, const int64_t* start, int64_t R, int H,
+                            void* out, int num_sms, cudaStream_t s);
 int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
                          const int64_t* start, int64_t U, const uint32_t* idx, int k, int E,
                          int G, int32_t* flat, int num_sms, cudaStream_t s);

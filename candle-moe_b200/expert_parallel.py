@@ -62,9 +62,8 @@ class CudaOps:
                                         num_ranks, n)
 
     @staticmethod
-    def local_experts(x, gate, up, down, w, e, num_local, activation, moe_type):
-        moe = candle_moe.FusedMoE(num_local, e.shape[1], candle_moe.Activation(activation))
-        return moe.forward(x, gate, up, down, w, e, moe_type)
+    def segment_sum(rows, start):
+        return candle_moe.segment_sum_rows(rows, start)
 
     @staticmethod
     def route_prep(groups_of_rows, w, groups):
@@ -222,16 +221,22 @@ class ExpertParallelMoE:
             computed += n_out
             e_loc = rm[:, :k].contiguous()
             w_loc = rm[:, k:].contiguous().view(torch.float32)
+            # every (row, slot) contribution, written consecutively in row-major order
+            n_asg = int(recv_asg[:, c].sum())
+            contrib = torch.empty((n_asg, H), dtype=x.dtype, device=dev)
+            if n_asg:
+                valid = e_loc < El
+                out_row = (torch.cumsum(valid.view(-1), 0) - 1).to(torch.int32)
+                self.ops.local_experts_scatter(rx, gate_local, up_local, down_local, w_loc,
+                                               e_loc, out_row, contrib, El, self.activation,
+                                               moe_type)
             if exact:
-                y = torch.empty((n_out, H), dtype=x.dtype, device=dev)
-                if n_out:
-                    out_row = (torch.cumsum((e_loc < El).view(-1), 0) - 1).to(torch.int32)
-                    self.ops.local_experts_scatter(rx, gate_local, up_local, down_local, w_loc,
-                                                   e_loc, out_row, y, El, self.activation,
-                                                   moe_type)
+                y = contrib
             elif R:
-                y = self.ops.local_experts(rx, gate_local, up_local, down_local, w_loc, e_loc,
-                                           El, self.activation, moe_type)
+                # partial of each received row: its consecutive contributions, in slot order
+                start = torch.zeros((R + 1,), dtype=torch.int64, device=dev)
+                torch.cumsum(valid.sum(dim=1), 0, out=start[1:])
+                y = self.ops.segment_sum(contrib, start)
             else:
                 y = torch.empty((0, H), dtype=x.dtype, device=dev)
             h3 = dist.all_to_all_single(back[back_off[c]:back_off[c + 1]], y,

@@ -154,6 +154,14 @@ int moe_ep_pack(const void* input, const int32_t* pair_token, const int32_t* pai
                 int64_t num_pairs, const uint32_t* expert_indices, const float* routing_weights,
                 int32_t topk, int32_t num_experts, int32_t num_ranks, int32_t hidden_dim,
                 uint32_t dtype, void* rows, int32_t* meta, int32_t* slot_count, void* stream);
+/*
+ * output[r, :] = sum of rows_in[segment_start[r] .. segment_start[r+1]) in row order, f32
+ * accumulation, one rounding to `dtype` (segment_start: num_segments + 1 int64 offsets).  The
+ * remote half of the expert-parallel "partials" return: a pair's slot contributions, written
+ * consecutively by moe_fused_scatter, become one partial row.
+ */
+int moe_segment_sum_rows(const void* rows_in, const int64_t* segment_start, int64_t num_segments,
+                         int32_t hidden_dim, uint32_t dtype, void* output, void* stream);
 int moe_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
                       const int64_t* pair_start, int64_t num_pairs,
                       const uint32_t* expert_indices, int32_t topk, int32_t num_experts,

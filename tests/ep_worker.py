@@ -69,14 +69,12 @@ class CpuOracleOps:
         return flat
 
     @staticmethod
-    def local_experts(x, gate, up, down, w, e, num_local, activation, moe_type):
-        if x.shape[0] == 0:
-            return torch.zeros_like(x)
-        out = oracle.moe_forward(x.numpy(), gate.numpy(), up.numpy(),
-                                 None if down is None else down.numpy(), w.numpy(),
-                                 e.numpy().astype(np.uint32), activation=activation,
-                                 moe_type=moe_type, dtype="f32")
-        return torch.from_numpy(out)
+    def segment_sum(rows, start):
+        out = torch.zeros((start.numel() - 1, rows.shape[1]), dtype=torch.float32)
+        for r in range(start.numel() - 1):
+            for i in range(int(start[r]), int(start[r + 1])):
+                out[r] += rows[i]
+        return out
 
     @staticmethod
     def route_prep(dest, w, groups):
