@@ -12,7 +12,8 @@
 //              cp.async copies written straight into the 128-byte-swizzled layout (a TMA
 //              tile::gather4 version of this producer measured 2-3x slower on B200), completion
 //              signalled with cp.async.mbarrier.arrive.  Warp 2 also owns the TMEM allocation.
-//   warp 1     one thread issues tcgen05.mma (M=128, N=128/256, K=16, f32 accumulate in TMEM)
+//   warp 1     one thread issues tcgen05.mma (M=128, N=128/256, K=16, f32 accumulate in TMEM;
+//              Qwen3's gate|up pair is one N=256 MMA whose accumulator holds both halves)
 //              and tcgen05.commit to release smem stages and publish accumulators.
 //   warps 4-7  epilogue: tcgen05.ld the accumulator (one TMEM lane per output row), apply the
 //              fused epilogue and store 64-byte row segments:
@@ -52,7 +53,9 @@ constexpr size_t kSm100SmemMax = 232448 - 1024;
 template <int MODE, int BN>
 struct TileCfg {
   static constexpr bool kGather = (MODE == kModeG1Dual || MODE == kModeG1Single);
-  static constexpr int kMmaN = (MODE == kModeG1Dual) ? 128 : BN;
+  // Qwen3's gate and up tiles sit back to back in shared memory (boxes 0-1 gate, 2-3 up, one
+  // 8 KB box stride), so one N=256 MMA computes both accumulators, reading the A tile once.
+  static constexpr int kMmaN = (MODE == kModeG1Dual) ? 256 : BN;
   static constexpr int kOutCols = (MODE == kModeG1Dual) ? 128 : BN;
   static constexpr int kBBytes = (MODE == kModeG1Dual) ? 2 * 128 * kBK * 2 : BN * kBK * 2;
   // bytes the TMA copies of one stage deliver (A too when it is not gathered)
@@ -268,10 +271,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           for (int ks = 0; ks < kBK / 16; ++ks) {
             const uint64_t adesc = umma_sdesc(a_base + ks * 32, 16, 1024);
             const uint32_t acc = (kb | ks) != 0 ? 1u : 0u;
-            if (MODE == kModeG1Dual) {
-              umma_f16(d, adesc, umma_sdesc(b_base + ks * 2048, 8192, 1024), idesc, acc);
-              umma_f16(d + 128, adesc, umma_sdesc(b_base + 16384 + ks * 2048, 8192, 1024), idesc, acc);
-            } else if (MODE == kModeG2K) {
+            if (MODE == kModeG2K) {
               umma_f16(d, adesc, umma_sdesc(b_base + ks * 32, 16, 1024), idesc, acc);
             } else {
               umma_f16(d, adesc, umma_sdesc(b_base + ks * 2048, 8192, 1024), idesc, acc);
