@@ -113,6 +113,25 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+_JSON_OUT = None
+
+
+def reserve_stdout():
+    """Keep stdout for the one JSON line: file descriptor 1 is pointed at stderr, so whatever
+    native libraries print (NCCL prints its version banner at every debug level from VERSION up)
+    lands there, and the JSON line is written to a saved copy of the original stdout."""
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(line):
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def dist_setup(n_gpus):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -121,9 +140,6 @@ def dist_setup(n_gpus):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # NCCL's version banner goes to stdout, which must carry only the one JSON line
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -355,7 +371,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not router_only:
         line["cpu_baseline"] = cpu_baseline(cfg, inp, target_s=args.cpu_seconds)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def cpu_baseline(cfg, inp, target_s=10.0):
@@ -442,7 +458,7 @@ def run_reference(args, world, rank):
         "note": "the reference crate has no CPU implementation; this is its algorithm restated "
                 "in C (oracle/) on the host cores",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -466,6 +482,7 @@ def main():
         CONFIGS[args.config] = CONFIGS[args.config][:3] + (args.tokens,) + CONFIGS[args.config][4:]
         WORKLOAD_NAMES[args.config] += f" [tokens overridden: {args.tokens}]"
     args.warmup = max(args.warmup, 3)
+    reserve_stdout()
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
