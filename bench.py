@@ -201,7 +201,7 @@ def run_ours(args, world, rank, local):
     if ep:
         import expert_parallel
         layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act),
-                                                  mode=args.ep_mode)
+                                                  mode=args.ep_mode, transport=args.ep_transport)
         if args.sm_reserve >= 0:
             layer.sm_reserve = args.sm_reserve
         inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
@@ -333,6 +333,7 @@ def run_ours(args, world, rank, local):
                    "intermediate": I, "experts": E, "top_k": k,
                    "parallelism": (f"ep{world}" if ep else "replicas") if world > 1 else "single-gpu",
                    "ep_mode": args.ep_mode if ep else None,
+                   "ep_transport": layer.transport if ep else None,
                    "tokens_per_rank": T,
                    "l2": "inputs larger than L2 (weights 1.2 GB + activations), no flush"
                    if args.config == "c5" else "no flush"},
@@ -345,6 +346,8 @@ def run_ours(args, world, rank, local):
         st, n = layer.stage_times()
         line["ep_stages_ms"] = {s_: v / max(n, 1) for s_, v in st.items()}
         line["ep_rows"] = {k_: int(v) for k_, v in layer.last_stats.items()}
+        if layer.transport == "p2p":
+            line["ep_timeline_ms"] = {k_: round(v, 3) for k_, v in layer.timeline().items()}
     if not router_only and ncalls:
         rows = layer.last_stats["assignments_received"] if ep else T * k
         n_up = 2 if moe_type == 0 else 1
@@ -370,6 +373,11 @@ def run_ours(args, world, rank, local):
                    "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's compute"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not router_only:
         line["cpu_baseline"] = cpu_baseline(cfg, inp, target_s=args.cpu_seconds)
+    if ep:
+        # non-zero when an arrival wait of the p2p exchange ran out (a rank never signalled)
+        line["device_error_bits"] = int(max_over_ranks(world,
+                                                       candle_moe.device_error_bits(local)))
+        layer.close()
     if rank == 0:
         emit(line)
 
@@ -473,6 +481,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-mode", choices=["partials", "exact"], default="partials",
                     help="expert-parallel return: per-rank partial sums or per-slot rows")
+    ap.add_argument("--ep-transport", choices=["p2p", "collective"], default="p2p",
+                    help="expert-parallel row exchange: copy engines into peer-mapped landing "
+                         "buffers, or NCCL all_to_all_single")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
     ap.add_argument("--tokens", type=int, default=0,

@@ -75,9 +75,9 @@ def lib() -> ctypes.CDLL:
         L.moe_fused_scatter.argtypes = [P, P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, U32,
                                          U32, P]
         L.moe_fused_scatter.restype = ctypes.c_int
-        L.moe_ep_dest_groups.argtypes = [P, I64, I32, I32, I32, I64, P, P]
+        L.moe_ep_dest_groups.argtypes = [P, I64, I32, I32, I32, I64, P, I32, P, P]
         L.moe_ep_dest_groups.restype = ctypes.c_int
-        L.moe_ep_pack.argtypes = [P, P, P, I64, P, P, I32, I32, I32, I32, U32, P, P, P, P]
+        L.moe_ep_pack.argtypes = [P, P, P, I64, P, P, P, I32, I32, I32, I32, U32, P, P, P, P]
         L.moe_ep_pack.restype = ctypes.c_int
         L.moe_ep_entry_flat.argtypes = [P, P, P, I64, P, I32, I32, I32, P, P]
         L.moe_ep_entry_flat.restype = ctypes.c_int
@@ -97,6 +97,21 @@ def lib() -> ctypes.CDLL:
         L.moe_phase_timing.restype = ctypes.c_int
         L.moe_phase_times.argtypes = [P, P]
         L.moe_phase_times.restype = ctypes.c_int
+        U8P = ctypes.POINTER(ctypes.c_uint8)
+        L.moe_peer_alloc.argtypes = [SZ, ctypes.POINTER(ctypes.c_void_p), U8P]
+        L.moe_peer_alloc.restype = ctypes.c_int
+        L.moe_peer_free.argtypes = [P]
+        L.moe_peer_free.restype = ctypes.c_int
+        L.moe_peer_open.argtypes = [U8P, ctypes.POINTER(ctypes.c_void_p)]
+        L.moe_peer_open.restype = ctypes.c_int
+        L.moe_peer_close.argtypes = [P]
+        L.moe_peer_close.restype = ctypes.c_int
+        L.moe_copy_async.argtypes = [P, P, SZ, P]
+        L.moe_copy_async.restype = ctypes.c_int
+        L.moe_peer_signal.argtypes = [ctypes.POINTER(ctypes.c_void_p), I32, U32, P]
+        L.moe_peer_signal.restype = ctypes.c_int
+        L.moe_peer_wait.argtypes = [P, I32, U32, I64, P]
+        L.moe_peer_wait.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -247,24 +262,30 @@ def route_prep_ex(expert_indices: torch.Tensor, routing_weights: torch.Tensor, n
 
 
 def ep_dest_groups(expert_indices: torch.Tensor, num_experts: int, num_ranks: int,
-                   tokens_per_chunk: int) -> torch.Tensor:
-    """[T, num_ranks] int32 group of each (token, rank) pair (see include/candle_moe.h)."""
+                   tokens_per_chunk: int, num_chunks: Optional[int] = None):
+    """[T, num_ranks] int32 group of each (token, rank) pair (see include/candle_moe.h); with
+    num_chunks, also the [num_chunks, num_ranks] int64 (token, slot) assignment counts."""
     _need_contig(expert_indices, "expert_indices")
     T, k = expert_indices.shape
     dev = expert_indices.device
     groups = torch.empty((T, num_ranks), dtype=torch.int32, device=dev)
+    asg = None if num_chunks is None else torch.empty((num_chunks, num_ranks), dtype=torch.int64,
+                                                      device=dev)
     with torch.cuda.device(dev):
         st = lib().moe_ep_dest_groups(_ptr(expert_indices), T, k, num_experts, num_ranks,
-                                      tokens_per_chunk, _ptr(groups), _stream(dev))
+                                      tokens_per_chunk, _ptr(groups), num_chunks or 0, _ptr(asg),
+                                      _stream(dev))
     if st != MOE_OK:
         raise MoeError(st, "moe_ep_dest_groups")
-    return groups
+    return groups if asg is None else (groups, asg)
 
 
 def ep_pack(x: torch.Tensor, pair_token: torch.Tensor, pair_flat: torch.Tensor,
             expert_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int,
-            num_ranks: int):
-    """(rows [U,H], meta [U, 2k] int32, slot_count [U] int32) of the U sorted pairs."""
+            num_ranks: int, num_pairs_device: Optional[torch.Tensor] = None):
+    """(rows [U,H], meta [U, 2k] int32, slot_count [U] int32) of the U = pair_token.numel()
+    sorted pairs; with num_pairs_device (an int32 on the GPU) only that many are packed and U is
+    the capacity."""
     U = pair_token.numel()
     T, k = expert_indices.shape
     H = x.shape[1]
@@ -274,7 +295,7 @@ def ep_pack(x: torch.Tensor, pair_token: torch.Tensor, pair_flat: torch.Tensor,
     count = torch.empty((U,), dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         st = lib().moe_ep_pack(_ptr(x), _ptr(pair_token), _ptr(pair_flat), U,
-                               _ptr(expert_indices), _ptr(routing_weights), k, num_experts,
+                               _ptr(num_pairs_device), _ptr(expert_indices), _ptr(routing_weights), k, num_experts,
                                num_ranks, H, fused_moe_internal_dtype(x.dtype), _ptr(rows),
                                _ptr(meta), _ptr(count), _stream(dev))
     if st != MOE_OK:
@@ -557,3 +578,87 @@ def phase_times():
     if st != MOE_OK:
         raise MoeError(st, "moe_phase_times")
     return {n: float(ms[i]) for i, n in enumerate(PHASES)}, int(calls.value)
+
+
+# ---------------------------------------------------------------------------------------------
+# peer-mapped buffers and arrival flags (expert-parallel exchange over NVLink)
+# ---------------------------------------------------------------------------------------------
+
+PEER_HANDLE_BYTES = 64
+ERR_PEER_WAIT = 64  # device error bit set by a peer_wait that ran out of time
+
+
+def peer_alloc(nbytes: int, device) -> tuple[int, bytes]:
+    """Zero-filled device memory on `device` that other processes can map: (pointer, handle)."""
+    ptr = ctypes.c_void_p()
+    h = (ctypes.c_uint8 * PEER_HANDLE_BYTES)()
+    with torch.cuda.device(device):
+        st = lib().moe_peer_alloc(nbytes, ctypes.byref(ptr), h)
+    if st != MOE_OK:
+        raise MoeError(st, f"moe_peer_alloc({nbytes})")
+    return int(ptr.value), bytes(h)
+
+
+def peer_free(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        st = lib().moe_peer_free(ctypes.c_void_p(ptr))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_peer_free")
+
+
+def peer_open(handle: bytes, device) -> int:
+    """Map another process's peer_alloc buffer on `device`; returns the local address."""
+    ptr = ctypes.c_void_p()
+    h = (ctypes.c_uint8 * PEER_HANDLE_BYTES).from_buffer_copy(handle)
+    with torch.cuda.device(device):
+        st = lib().moe_peer_open(h, ctypes.byref(ptr))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_peer_open")
+    return int(ptr.value)
+
+
+def peer_close(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        st = lib().moe_peer_close(ctypes.c_void_p(ptr))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_peer_close")
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream: torch.cuda.Stream) -> None:
+    """Copy nbytes from device address src to dst on `stream` (copy engine; peers allowed)."""
+    st = lib().moe_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
+                              ctypes.c_void_p(stream.cuda_stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_copy_async")
+
+
+def peer_signal(flag_addrs, value: int, stream: torch.cuda.Stream) -> None:
+    """Release-store `value` into each 32-bit flag at the device addresses flag_addrs."""
+    n = len(flag_addrs)
+    arr = (ctypes.c_void_p * max(n, 1))(*flag_addrs)
+    st = lib().moe_peer_signal(arr, n, value & 0xffffffff, ctypes.c_void_p(stream.cuda_stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_peer_signal")
+
+
+def peer_wait(flags: int, count: int, value: int, timeout_s: float,
+              stream: torch.cuda.Stream) -> None:
+    """Stream-ordered wait until the count flags at device address `flags` reach `value`; after
+    timeout_s the stream continues and device_error_bits() reports ERR_PEER_WAIT."""
+    st = lib().moe_peer_wait(ctypes.c_void_p(flags), count, value & 0xffffffff,
+                             int(timeout_s * 1e9), ctypes.c_void_p(stream.cuda_stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_peer_wait")
+
+
+class _RawDeviceMemory:
+    """Exposes nbytes at a device address through __cuda_array_interface__ (no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 2}
+
+
+def device_bytes(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over memory this module allocated (the caller keeps it alive)."""
+    return torch.as_tensor(_RawDeviceMemory(ptr, nbytes), device=device)

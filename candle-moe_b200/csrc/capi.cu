@@ -512,27 +512,30 @@ CMOE_API int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, 
 
 CMOE_API int moe_ep_dest_groups(const uint32_t* expert_indices, int64_t num_tokens, int32_t topk,
                                 int32_t num_experts, int32_t num_ranks,
-                                int64_t tokens_per_chunk, int32_t* groups, void* stream) {
+                                int64_t tokens_per_chunk, int32_t* groups, int32_t num_chunks,
+                                int64_t* assignment_counts, void* stream) {
   if (num_tokens < 0 || topk <= 0 || num_experts <= 0 || num_ranks <= 0 || tokens_per_chunk <= 0)
     return MOE_ERR_INVALID_ARG;
-  if (num_tokens == 0) return MOE_OK;
-  if (!expert_indices || !groups) return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0 && !assignment_counts) return MOE_OK;
+  if ((num_tokens > 0 && (!expert_indices || !groups)) || (assignment_counts && num_chunks <= 0))
+    return MOE_ERR_INVALID_ARG;
   DeviceState* ds = nullptr;
   int st = current_device_state(&ds);
   if (st != MOE_OK) return st;
   if (launch_ep_dest_groups(expert_indices, num_tokens, topk, num_experts, num_ranks,
-                            tokens_per_chunk, groups, ds->num_sms,
+                            tokens_per_chunk, groups, assignment_counts, num_chunks, ds->num_sms,
                             static_cast<cudaStream_t>(stream)))
     return MOE_ERR_UNSUPPORTED;
-  ++g_launches;
+  if (num_tokens > 0) ++g_launches;
   return finish(MOE_OK);
 }
 
 CMOE_API int moe_ep_pack(const void* input, const int32_t* pair_token, const int32_t* pair_flat,
-                         int64_t num_pairs, const uint32_t* expert_indices,
-                         const float* routing_weights, int32_t topk, int32_t num_experts,
-                         int32_t num_ranks, int32_t hidden_dim, uint32_t dtype, void* rows,
-                         int32_t* meta, int32_t* slot_count, void* stream) {
+                         int64_t num_pairs, const int32_t* num_pairs_device,
+                         const uint32_t* expert_indices, const float* routing_weights,
+                         int32_t topk, int32_t num_experts, int32_t num_ranks,
+                         int32_t hidden_dim, uint32_t dtype, void* rows, int32_t* meta,
+                         int32_t* slot_count, void* stream) {
   if (num_pairs < 0 || topk <= 0 || num_experts <= 0 || num_ranks <= 0 || hidden_dim <= 0 ||
       dtype > 2)
     return MOE_ERR_INVALID_ARG;
@@ -544,7 +547,8 @@ CMOE_API int moe_ep_pack(const void* input, const int32_t* pair_token, const int
   int st = current_device_state(&ds);
   if (st != MOE_OK) return st;
   if (launch_ep_pack(static_cast<int>(dtype), input, pair_token, pair_flat, num_pairs,
-                     expert_indices, routing_weights, topk, num_experts, num_ranks, hidden_dim,
+                     num_pairs_device, expert_indices, routing_weights, topk, num_experts,
+                     num_ranks, hidden_dim,
                      rows, meta, slot_count, ds->num_sms, static_cast<cudaStream_t>(stream)))
     return MOE_ERR_UNSUPPORTED;
   ++g_launches;
@@ -688,3 +692,104 @@ CMOE_API int moe_phase_times(double* ms, int64_t* calls) {
   if (calls) *calls = g_timer.calls;
   return MOE_OK;
 }
+
+// ---- peer-mapped buffers and arrival flags (expert-parallel exchange) ------------------------
+
+static_assert(sizeof(cudaIpcMemHandle_t) == MOE_PEER_HANDLE_BYTES, "IPC handle size");
+
+CMOE_API int moe_peer_alloc(size_t bytes, void** ptr, uint8_t* handle) {
+  if (!ptr || !handle || bytes == 0) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_NO_MEMORY;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return MOE_ERR_CUDA;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return MOE_OK;
+}
+
+CMOE_API int moe_peer_free(void* ptr) {
+  if (!ptr) return MOE_ERR_INVALID_ARG;
+  return finish(cudaFree(ptr) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA);
+}
+
+CMOE_API int moe_peer_open(const uint8_t* handle, void** ptr) {
+  if (!handle || !ptr) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_CUDA;
+  }
+  *ptr = p;
+  return MOE_OK;
+}
+
+CMOE_API int moe_peer_close(void* ptr) {
+  if (!ptr) return MOE_ERR_INVALID_ARG;
+  if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_CUDA;
+  }
+  return MOE_OK;
+}
+
+CMOE_API int moe_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return MOE_OK;
+  if (!dst || !src) return MOE_ERR_INVALID_ARG;
+  if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return MOE_ERR_CUDA;
+  }
+  return MOE_OK;
+}
+
+CMOE_API int moe_peer_signal(uint32_t* const* flag_addrs, int32_t count, uint32_t value,
+                             void* stream) {
+  if (count < 0 || count > kMaxPeerFlags || (count > 0 && !flag_addrs))
+    return MOE_ERR_INVALID_ARG;
+  if (count == 0) return MOE_OK;
+  PeerFlagPtrs t{};
+  for (int i = 0; i < count; ++i) {
+    if (!flag_addrs[i] || (reinterpret_cast<uintptr_t>(flag_addrs[i]) & 3u))
+      return MOE_ERR_INVALID_ARG;
+    t.p[i] = flag_addrs[i];
+  }
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  launch_peer_signal(t, count, value, static_cast<cudaStream_t>(stream));
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_peer_wait(const uint32_t* flags, int32_t count, uint32_t value,
+                           int64_t timeout_ns, void* stream) {
+  if (count < 0 || count > kMaxPeerFlags || timeout_ns <= 0 || (count > 0 && !flags) ||
+      (reinterpret_cast<uintptr_t>(flags) & 3u))
+    return MOE_ERR_INVALID_ARG;
+  if (count == 0) return MOE_OK;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  launch_peer_wait(flags, count, value, static_cast<unsigned long long>(timeout_ns), ds->err_word,
+                   static_cast<cudaStream_t>(stream));
+  ++g_launches;
+  return finish(MOE_OK);
+}
+

@@ -27,6 +27,7 @@ enum DevErr : uint32_t {
   kErrWaitAccEmpty = 8u,  // MMA issuer gave up waiting for an accumulator to drain
   kErrWaitDrain = 16u,    // teardown gave up waiting for copies in flight
   kErrTmemAlloc = 32u,    // TMEM allocation returned an unusable address
+  kErrPeerWait = 64u,     // an expert-parallel arrival flag was not reached in time
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -228,6 +229,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr)
       : "memory");
 }
+// Orders shared-memory writes made through the generic proxy (st.shared, non-bulk cp.async)
+// before later async-proxy accesses (tcgen05.mma operand reads, TMA) in the causality chain.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

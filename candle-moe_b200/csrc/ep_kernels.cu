@@ -5,6 +5,7 @@
 // [T,k] expert ids into (token, rank) pairs, pack the pairs' rows and slot metadata for the
 // all-to-all, and map the contributions that come back to the token slots they belong to.
 #include <stdint.h>
+#include <climits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -12,22 +13,38 @@
 namespace cmoe {
 
 // groups[t*G + d] = (t / tokens_per_chunk) * G + d when token t has an expert on rank d, else
-// chunks*G (ignored by route preparation).  Ids >= E (skipped everywhere) select no rank.
+// INT32_MAX (above any group count, so route preparation ignores it).  Ids >= E (skipped
+// everywhere) select no rank.
+// With `asg` (nbins = chunks * G counters, zeroed by the caller), also counts the (token, slot)
+// assignments per (chunk, rank): per-block shared-memory histogram, one global add per bin.
 __global__ void __launch_bounds__(256) ep_dest_groups_kernel(const uint32_t* __restrict__ idx,
                                                              int64_t T, int k, int E, int El,
                                                              int G, int64_t tokens_per_chunk,
-                                                             int32_t* __restrict__ groups) {
+                                                             int32_t* __restrict__ groups,
+                                                             unsigned long long* asg, int nbins) {
+  extern __shared__ int s_hist[];
+  if (asg) {
+    for (int i = threadIdx.x; i < nbins; i += blockDim.x) s_hist[i] = 0;
+    __syncthreads();
+  }
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < T;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     uint32_t mask = 0;  // G <= 32
+    const int32_t chunk = static_cast<int32_t>(t / tokens_per_chunk);
     for (int j = 0; j < k; ++j) {
       const uint32_t e = __ldg(idx + t * k + j);
-      if (e < static_cast<uint32_t>(E)) mask |= 1u << (e / El);
+      if (e < static_cast<uint32_t>(E)) {
+        mask |= 1u << (e / El);
+        if (asg) atomicAdd(&s_hist[chunk * G + static_cast<int>(e / El)], 1);
+      }
     }
-    const int32_t chunk = static_cast<int32_t>(t / tokens_per_chunk);
-    const int32_t chunks_g = static_cast<int32_t>(((T + tokens_per_chunk - 1) / tokens_per_chunk) * G);
     for (int d = 0; d < G; ++d)
-      groups[t * G + d] = (mask >> d) & 1u ? chunk * G + d : chunks_g;
+      groups[t * G + d] = (mask >> d) & 1u ? chunk * G + d : INT32_MAX;
+  }
+  if (asg) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < nbins; i += blockDim.x)
+      if (s_hist[i]) atomicAdd(asg + i, static_cast<unsigned long long>(s_hist[i]));
   }
 }
 
@@ -35,12 +52,16 @@ __global__ void __launch_bounds__(256) ep_dest_groups_kernel(const uint32_t* __r
 // rows[r] (one warp per pair, 16-byte lanes) and write the pair's slot metadata: meta[r*2k + j] =
 // local expert id of slot j if that slot's expert lives on rank d, else El; meta[r*2k + k + j] =
 // the slot's routing weight bits (0 for foreign slots).  count[r] = slots of the pair.
+// With n_dev, the pair count is read from device memory (at most U, the capacity), so the pack
+// can be enqueued before the host knows the count.
 template <typename V>
 __global__ void __launch_bounds__(256) ep_pack_kernel(
     const V* __restrict__ x, const int32_t* __restrict__ pair_token,
-    const int32_t* __restrict__ pair_flat, int64_t U, const uint32_t* __restrict__ idx,
-    const float* __restrict__ w, int k, int E, int El, int G, int vec_per_row,
-    V* __restrict__ rows, int32_t* __restrict__ meta, int32_t* __restrict__ count) {
+    const int32_t* __restrict__ pair_flat, int64_t U, const int32_t* __restrict__ n_dev,
+    const uint32_t* __restrict__ idx, const float* __restrict__ w, int k, int E, int El, int G,
+    int vec_per_row, V* __restrict__ rows, int32_t* __restrict__ meta,
+    int32_t* __restrict__ count) {
+  if (n_dev) U = min(U, static_cast<int64_t>(max(__ldg(n_dev), 0)));
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -143,18 +164,24 @@ static unsigned ep_grid(int64_t work, int num_sms) {
 }
 
 int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,
-                          int64_t tokens_per_chunk, int32_t* groups, int num_sms,
-                          cudaStream_t s) {
+                          int64_t tokens_per_chunk, int32_t* groups, int64_t* asg, int chunks,
+                          int num_sms, cudaStream_t s) {
   if (G < 1 || G > 32 || E % G != 0 || tokens_per_chunk < 1) return 1;
+  const int nbins = asg ? chunks * G : 0;
+  if (asg && (chunks < 1 || nbins > kMaxEpBins || (T + tokens_per_chunk - 1) / tokens_per_chunk > chunks))
+    return 1;
+  if (asg && cudaMemsetAsync(asg, 0, sizeof(int64_t) * nbins, s) != cudaSuccess) return 1;
   if (T <= 0) return 0;
-  ep_dest_groups_kernel<<<ep_grid(T, num_sms), 256, 0, s>>>(idx, T, k, E, E / G, G,
-                                                            tokens_per_chunk, groups);
+  ep_dest_groups_kernel<<<ep_grid(T, num_sms), 256, nbins * sizeof(int), s>>>(
+      idx, T, k, E, E / G, G, tokens_per_chunk, groups,
+      reinterpret_cast<unsigned long long*>(asg), nbins);
   return 0;
 }
 
 int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const int32_t* pair_flat,
-                   int64_t U, const uint32_t* idx, const float* w, int k, int E, int G, int H,
-                   void* rows, int32_t* meta, int32_t* count, int num_sms, cudaStream_t s) {
+                   int64_t U, const int32_t* n_dev, const uint32_t* idx, const float* w, int k,
+                   int E, int G, int H, void* rows, int32_t* meta, int32_t* count, int num_sms,
+                   cudaStream_t s) {
   if (G < 1 || G > 32 || E % G != 0 || k > 32) return 1;
   if (U <= 0) return 0;
   const size_t row_bytes = static_cast<size_t>(H) * (dtype == kF32 ? 4 : 2);
@@ -162,11 +189,11 @@ int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const in
   if (row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(rows) % 16 == 0)
     ep_pack_kernel<uint4><<<grid, 256, 0, s>>>(
-        static_cast<const uint4*>(x), pair_token, pair_flat, U, idx, w, k, E, E / G, G,
+        static_cast<const uint4*>(x), pair_token, pair_flat, U, n_dev, idx, w, k, E, E / G, G,
         static_cast<int>(row_bytes / 16), static_cast<uint4*>(rows), meta, count);
   else
     ep_pack_kernel<uint16_t><<<grid, 256, 0, s>>>(
-        static_cast<const uint16_t*>(x), pair_token, pair_flat, U, idx, w, k, E, E / G, G,
+        static_cast<const uint16_t*>(x), pair_token, pair_flat, U, n_dev, idx, w, k, E, E / G, G,
         static_cast<int>(row_bytes / 2), static_cast<uint16_t*>(rows), meta, count);
   return 0;
 }

@@ -82,16 +82,27 @@ int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const C
                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
 
 // ---- ep_kernels.cu -------------------------------------------------------------------------
+constexpr int kMaxEpBins = 12288;  // (chunk, rank) counters of ep_dest_groups (48 KB smem)
 int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,
-                          int64_t tokens_per_chunk, int32_t* groups, int num_sms,
-                          cudaStream_t s);
+                          int64_t tokens_per_chunk, int32_t* groups, int64_t* asg, int chunks,
+                          int num_sms, cudaStream_t s);
 int launch_ep_pack(int dtype, const void* x, const int32_t* pair_token, const int32_t* pair_flat,
-                   int64_t U, const uint32_t* idx, const float* w, int k, int E, int G, int H,
-                   void* rows, int32_t* meta, int32_t* count, int num_sms, cudaStream_t s);
+                   int64_t U, const int32_t* n_dev, const uint32_t* idx, const float* w, int k,
+                   int E, int G, int H, void* rows, int32_t* meta, int32_t* count, int num_sms,
+                   cudaStream_t s);
 int launch_segment_sum_rows(int dtype, const void* in, const int64_t* start, int64_t R, int H,
                             void* out, int num_sms, cudaStream_t s);
 int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
                          const int64_t* start, int64_t U, const uint32_t* idx, int k, int E,
                          int G, int32_t* flat, int num_sms, cudaStream_t s);
+
+// arrival flags of the expert-parallel exchange (peer.cu)
+constexpr int kMaxPeerFlags = 64;
+struct PeerFlagPtrs {
+  uint32_t* p[kMaxPeerFlags];
+};
+int launch_peer_signal(const PeerFlagPtrs& targets, int count, uint32_t value, cudaStream_t s);
+int launch_peer_wait(const uint32_t* flags, int count, uint32_t value,
+                     unsigned long long timeout_ns, uint32_t* err, cudaStream_t s);
 
 }  // namespace cmoe

@@ -264,6 +264,9 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             ok = false;
             break;
           }
+          // the gathered A rows were written by cp.async (generic proxy); the MMA reads them
+          // through the async proxy
+          if (C::kGather) fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t a_base = smem_base + stage * kStageBytes;
           const uint32_t b_base = a_base + kAStageBytes;
@@ -379,6 +382,14 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       const int unit = lane & 7;
 #pragma unroll 1
       for (int cc = 0; cc < C::kOutCols; cc += 64) {
+        // one accumulator slab: Qwen3's gate and up halves are loaded per 32 columns; the single
+        // accumulators load all 64 columns before one wait
+        uint32_t a[2][32];
+        if (MODE != kModeG1Dual) {
+          tmem_ld_32x32b_x32(tb + cc, a[0]);
+          tmem_ld_32x32b_x32(tb + cc + 32, a[1]);
+          tmem_ld_wait();
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float v[32];
@@ -390,17 +401,12 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               v[i] = act_apply(__uint_as_float(gv[i]), p.act) * __uint_as_float(uv[i]);
+          } else if (MODE == kModeG1Single) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(a[h][i]), p.act);
           } else {
-            uint32_t a[32];
-            tmem_ld_32x32b_x32(tb + cc + 32 * h, a);
-            tmem_ld_wait();
-            if (MODE == kModeG1Single) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = act_apply(__uint_as_float(a[i]), p.act);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) * wgt;
-            }
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[h][i]) * wgt;
           }
           // this thread's row (lane) holds units 4h..4h+3 of the 64-column slab
 #pragma unroll

@@ -7,8 +7,9 @@
 // are those of the reference launcher (topk_softmax.cu:268-295), and this file is compiled with
 // --use_fast_math like the reference build (build.rs:59), so the weights come out bit-identical
 // to the reference kernel's.  Differences from the reference: a grid-stride loop sized to the
-// SM count instead of one CTA per 4 warps of rows, an optional renormalisation of the k weights
-// (Qwen3 norm_topk_prob), and a status return for unsupported expert counts.
+// SM count instead of one CTA per 4 warps of rows, picks made with two warp reductions per round
+// when a warp owns the row (same picks; see below), an optional renormalisation of the k
+// weights (Qwen3 norm_topk_prob), and a status return for unsupported expert counts.
 #include <stdint.h>
 
 #include "common.cuh"
@@ -27,6 +28,16 @@ struct RouterGeom {
 };
 
 template <int N> struct alignas(4 * N) FVec { float v[N]; };
+
+// Order-preserving map of non-NaN floats to 32-bit unsigned keys (a < b  <=>  key(a) < key(b))
+// and its inverse; equal floats other than +-0 have equal bits.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float from_order_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
 template <int E>
 __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
@@ -89,27 +100,48 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
       pw[s2] = 0.f;
       pe[s2] = 0;
     }
+    // When one warp owns the row and its probabilities are numbers, each round is two warp
+    // reductions in hardware: the largest value (as an order-preserving 32-bit key), then the
+    // lowest expert holding it -- the same pick as the shuffle argmax, which rows with NaN
+    // probabilities keep (its picks there depend on the lane order, as in the reference).
+    const bool redux = kTpr == 32 && (__float_as_uint(s) & 0x7fffffffu) <= 0x7f800000u;
     for (int j = 0; j < k; ++j) {
-      float best = v[0];
-      int be = col0;
+      float best;
+      int be;
+      if (redux) {
+        uint32_t kl = 0;
 #pragma unroll
-      for (int l = 0; l < kVecs; ++l) {
+        for (int i = 0; i < kVpt; ++i) kl = max(kl, order_key(v[i]));
+        const uint32_t km = __reduce_max_sync(0xffffffffu, kl);
+        uint32_t cand = 0xffffffffu;
 #pragma unroll
-        for (int i = 0; i < kElts; ++i) {
-          const float x = v[l * kElts + i];
-          if (x > best) {
-            best = x;
-            be = col0 + l * kElts * kTpr + i;
+        for (int i = kVpt - 1; i >= 0; --i)  // ascending expert ids: the first match is the lowest
+          if (order_key(v[i]) == km)
+            cand = static_cast<uint32_t>(col0 + (i / kElts) * kElts * kTpr + i % kElts);
+        be = static_cast<int>(__reduce_min_sync(0xffffffffu, cand));
+        best = from_order_key(km);
+      } else {
+        best = v[0];
+        be = col0;
+#pragma unroll
+        for (int l = 0; l < kVecs; ++l) {
+#pragma unroll
+          for (int i = 0; i < kElts; ++i) {
+            const float x = v[l * kElts + i];
+            if (x > best) {
+              best = x;
+              be = col0 + l * kElts * kTpr + i;
+            }
           }
         }
-      }
 #pragma unroll
-      for (int mask = kTpr / 2; mask > 0; mask /= 2) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, mask, kTpr);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, mask, kTpr);
-        if (ob > best || (ob == best && oe < be)) {
-          best = ob;
-          be = oe;
+        for (int mask = kTpr / 2; mask > 0; mask /= 2) {
+          const float ob = __shfl_xor_sync(0xffffffffu, best, mask, kTpr);
+          const int oe = __shfl_xor_sync(0xffffffffu, be, mask, kTpr);
+          if (ob > best || (ob == best && oe < be)) {
+            best = ob;
+            be = oe;
+          }
         }
       }
       wsum += best;

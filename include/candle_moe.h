@@ -136,24 +136,31 @@ int moe_combine_rows(const void* rows_buf, const int32_t* sorted_flat, int64_t r
  * With num_ranks ranks owning num_experts/num_ranks experts each:
  *
  * moe_ep_dest_groups: groups[t*num_ranks + d] = (t / tokens_per_chunk) * num_ranks + d when
- *   token t has one of its topk experts on rank d, else (number of chunks) * num_ranks; route
- *   preparation over these groups buckets the (token, rank) pairs to send.
+ *   token t has one of its topk experts on rank d, else INT32_MAX (no group); route
+ *   preparation over these groups buckets the (token, rank) pairs to send.  With
+ *   assignment_counts (else NULL), also writes the number of (token, slot) assignments to
+ *   experts of rank d among the tokens of chunk c to assignment_counts[c*num_ranks + d]
+ *   (num_chunks * num_ranks <= 12288 counters; every token's chunk must be < num_chunks).
  * moe_ep_pack: for the num_pairs sorted pairs (pair_token[r] = t, pair_flat[r] = t*num_ranks + d)
  *   copy input row t to rows[r], write the pair's topk-slot metadata (meta[r*2*topk + j] = local
  *   expert id of slot j if its expert lives on rank d, else num_experts/num_ranks;
  *   meta[r*2*topk + topk + j] = that slot's routing weight bits, or 0) and slot_count[r] = the
- *   pair's slots.
+ *   pair's slots.  With num_pairs_device (else NULL) the pair count is read from that device
+ *   int32 when the kernel runs and num_pairs is only the capacity of the outputs, so the pack
+ *   can be enqueued before the host has the count.
  * moe_ep_entry_flat: with pair_start the exclusive prefix of slot_count, write
  *   flat[pair_start[r] + i] = t*topk + j for the pair's i-th slot j (the token slot of each
  *   per-slot contribution returned for pair r).
  */
 int moe_ep_dest_groups(const uint32_t* expert_indices, int64_t num_tokens, int32_t topk,
                        int32_t num_experts, int32_t num_ranks, int64_t tokens_per_chunk,
-                       int32_t* groups, void* stream);
+                       int32_t* groups, int32_t num_chunks, int64_t* assignment_counts,
+                       void* stream);
 int moe_ep_pack(const void* input, const int32_t* pair_token, const int32_t* pair_flat,
-                int64_t num_pairs, const uint32_t* expert_indices, const float* routing_weights,
-                int32_t topk, int32_t num_experts, int32_t num_ranks, int32_t hidden_dim,
-                uint32_t dtype, void* rows, int32_t* meta, int32_t* slot_count, void* stream);
+                int64_t num_pairs, const int32_t* num_pairs_device,
+                const uint32_t* expert_indices, const float* routing_weights, int32_t topk,
+                int32_t num_experts, int32_t num_ranks, int32_t hidden_dim, uint32_t dtype,
+                void* rows, int32_t* meta, int32_t* slot_count, void* stream);
 /*
  * output[r, :] = sum of rows_in[segment_start[r] .. segment_start[r+1]) in row order, f32
  * accumulation, one rounding to `dtype` (segment_start: num_segments + 1 int64 offsets).  The
@@ -255,6 +262,32 @@ int moe_route_prep_noalloc(const uint32_t* expert_indices, const float* routing_
                            int64_t num_tokens, int32_t topk, int32_t num_experts,
                            int32_t* expert_offsets, int32_t* sorted_token_ids,
                            float* sorted_weights, void* stream);
+
+/*
+ * Peer-mapped buffers and arrival flags for the expert-parallel exchange over NVLink (no
+ * counterpart in the reference, which has no multi-GPU path).  Rows move by copy engine into a
+ * peer's landing buffer (moe_copy_async), so the exchange uses no SMs.
+ *
+ * moe_peer_alloc: device memory on the current device that other processes can map, zero-filled;
+ *   writes the pointer and a MOE_PEER_HANDLE_BYTES-byte handle to pass to the other ranks.
+ * moe_peer_free: frees a moe_peer_alloc buffer (after every peer has closed its mapping).
+ * moe_peer_open / moe_peer_close: map / unmap another process's buffer on the current device.
+ * moe_copy_async: `bytes` from src to dst on `stream` (either side may be a peer mapping).
+ * moe_peer_signal: after the work before it on `stream`, stores `value` with release semantics
+ *   (system scope) to each of the `count` (<= 64) 32-bit flags flag_addrs[0..count).
+ * moe_peer_wait: stream-ordered wait until every flags[i] (i < count <= 64) has reached `value`
+ *   (flag - value >= 0 as int32); after timeout_ns it sets bit 64 of the device error word
+ *   (moe_device_error_bits) and lets the stream continue.
+ */
+#define MOE_PEER_HANDLE_BYTES 64
+int moe_peer_alloc(size_t bytes, void** ptr, uint8_t* handle);
+int moe_peer_free(void* ptr);
+int moe_peer_open(const uint8_t* handle, void** ptr);
+int moe_peer_close(void* ptr);
+int moe_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+int moe_peer_signal(uint32_t* const* flag_addrs, int32_t count, uint32_t value, void* stream);
+int moe_peer_wait(const uint32_t* flags, int32_t count, uint32_t value, int64_t timeout_ns,
+                  void* stream);
 
 #ifdef __cplusplus
 }

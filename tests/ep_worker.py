@@ -1,6 +1,10 @@
 """Worker bodies of the expert-parallel tests (spawned ranks)."""
+import ctypes
+import mmap
 import os
 import socket
+import time
+import uuid
 
 import numpy as np
 import torch
@@ -21,24 +25,26 @@ class CpuOracleOps:
     and MoE, torch indexing for row movement and bookkeeping."""
 
     @staticmethod
-    def dest_groups(idx, num_experts, num_ranks, tokens_per_chunk):
+    def dest_groups(idx, num_experts, num_ranks, tokens_per_chunk, num_chunks):
         T, k = idx.shape
         El = num_experts // num_ranks
-        chunks = (T + tokens_per_chunk - 1) // tokens_per_chunk
-        g = torch.full((T, num_ranks), chunks * num_ranks, dtype=torch.int32)
+        g = torch.full((T, num_ranks), 0x7FFFFFFF, dtype=torch.int32)  # no group
+        asg = torch.zeros((num_chunks, num_ranks), dtype=torch.int64)
         for t in range(T):
             for j in range(k):
                 e = int(idx[t, j])
                 if 0 <= e < num_experts:
                     d = e // El
                     g[t, d] = (t // tokens_per_chunk) * num_ranks + d
-        return g
+                    asg[t // tokens_per_chunk, d] += 1
+        return g, asg
 
     @staticmethod
-    def pack(x, pair_token, pair_flat, idx, w, num_experts, num_ranks):
+    def pack(x, pair_token, pair_flat, idx, w, num_experts, num_ranks, num_pairs_device=None):
         El = num_experts // num_ranks
         k = idx.shape[1]
-        U = pair_token.numel()
+        U = pair_token.numel() if num_pairs_device is None else int(num_pairs_device[0])
+        pair_token, pair_flat = pair_token[:U], pair_flat[:U]
         rows = x[pair_token.long()].clone()
         meta = torch.zeros((U, 2 * k), dtype=torch.int32)
         meta[:, :k] = El
@@ -107,6 +113,91 @@ class CpuOracleOps:
     def set_sm_reserve(sms):
         return 0
 
+    # ---- p2p transport over host shared memory: each landing buffer is a file in /dev/shm that
+    # every rank maps; copies are memmoves, flags 32-bit stores and polls (x86 keeps the order)
+    _maps = {}
+
+    @classmethod
+    def _map(cls, path, nbytes, owner):
+        with open(path, "r+b") as f:
+            mm = mmap.mmap(f.fileno(), nbytes)
+        c = ctypes.c_char.from_buffer(mm)
+        addr = ctypes.addressof(c)
+        del c
+        cls._maps[addr] = (mm, path, owner)
+        return addr
+
+    @classmethod
+    def peer_alloc(cls, nbytes, device):
+        path = f"/dev/shm/cmoe_ep_test_{os.getpid()}_{uuid.uuid4().hex[:16]}"
+        with open(path, "wb") as f:
+            f.truncate(nbytes)
+        addr = cls._map(path, nbytes, True)
+        return addr, path.encode().ljust(64, b"\0")
+
+    @classmethod
+    def peer_open(cls, handle, device):
+        path = handle.rstrip(b"\0").decode()
+        return cls._map(path, os.path.getsize(path), False)
+
+    @classmethod
+    def peer_close(cls, addr, device):
+        mm, _, _ = cls._maps.pop(addr)
+        mm.close()
+
+    @classmethod
+    def peer_free(cls, addr, device):
+        mm, path, _ = cls._maps.pop(addr)
+        try:
+            mm.close()
+        except BufferError:  # a tensor view is still alive; the mapping goes with it
+            pass
+        os.unlink(path)
+
+    @classmethod
+    def device_bytes(cls, addr, nbytes, device):
+        return torch.frombuffer(cls._maps[addr][0], dtype=torch.uint8, count=nbytes)
+
+    @staticmethod
+    def copy_async(dst, src, nbytes, stream):
+        ctypes.memmove(dst, src, nbytes)
+
+    @staticmethod
+    def peer_signal(flag_addrs, value, stream):
+        for a in flag_addrs:
+            ctypes.c_uint32.from_address(a).value = value & 0xFFFFFFFF
+
+    @staticmethod
+    def peer_wait(flags, count, value, timeout_s, stream):
+        t0 = time.monotonic()
+        for i in range(count):
+            f = ctypes.c_uint32.from_address(flags + 4 * i)
+            while ((f.value - value) & 0xFFFFFFFF) >= 0x80000000:
+                if time.monotonic() - t0 > timeout_s:
+                    raise TimeoutError(f"flag {i} never reached {value}")
+                time.sleep(0.0002)
+
+    @staticmethod
+    def host_counts(work, gathered):
+        work.wait()
+        return torch.stack(gathered).numpy()
+
+    @staticmethod
+    def new_stream(device):
+        return None
+
+    @staticmethod
+    def current_stream(device):
+        return None
+
+    @staticmethod
+    def record(stream):
+        return None
+
+    @staticmethod
+    def wait(stream, event):
+        pass
+
     @staticmethod
     def combine_rows(rows, flat, num_tokens, k):
         out = torch.zeros((num_tokens, rows.shape[1]), dtype=torch.float32)
@@ -119,7 +210,10 @@ class CpuOracleOps:
         return out
 
 
-def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact"):
+def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
+             transport="collective", sizes=None):
+    """One CPU rank: forward the rank's tokens (the first n of its T for each n in `sizes`, in
+    order, through one layer) and report the worst error against the single-process oracle."""
     import expert_parallel
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -128,27 +222,35 @@ def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact")
         case = moe_case(17, T=T * world, H=H, I=I, E=E, k=k, moe_type=moe_type, dtype="f32",
                         wstd=0.1)
         case["idx"][::11, -1] = E  # an out-of-range id: skipped everywhere
-        lo, hi = rank * T, (rank + 1) * T
         e0, e1 = expert_parallel.expert_range(E, world, rank)
+        expert_parallel._Landing.SLACK_ROWS = 0  # let a larger second forward grow the buffers
         layer = expert_parallel.ExpertParallelMoE(E, k, 0, ops=CpuOracleOps(), chunks=3,
-                                                  mode=mode)
-        out = layer.forward(torch.from_numpy(case["x"][lo:hi].copy()),
-                            torch.from_numpy(case["gate"][e0:e1].copy()),
-                            torch.from_numpy(case["up"][e0:e1].copy()),
-                            None if case["down"] is None else torch.from_numpy(case["down"][e0:e1].copy()),
-                            torch.from_numpy(case["w"][lo:hi].copy()),
-                            torch.from_numpy(case["idx"][lo:hi].copy()), moe_type)
-        ref = oracle.moe_forward(case["x"][lo:hi].copy(), case["gate"], case["up"], case["down"],
-                                 case["w"][lo:hi].copy(), case["idx"][lo:hi].copy(), activation=0,
-                                 moe_type=moe_type, dtype="f32")
+                                                  mode=mode, transport=transport)
+        worst = 0.0
+        for n in sizes or [T]:
+            lo, hi = rank * T, rank * T + n
+            out = layer.forward(torch.from_numpy(case["x"][lo:hi].copy()),
+                                torch.from_numpy(case["gate"][e0:e1].copy()),
+                                torch.from_numpy(case["up"][e0:e1].copy()),
+                                None if case["down"] is None else
+                                torch.from_numpy(case["down"][e0:e1].copy()),
+                                torch.from_numpy(case["w"][lo:hi].copy()),
+                                torch.from_numpy(case["idx"][lo:hi].copy()), moe_type)
+            ref = oracle.moe_forward(case["x"][lo:hi].copy(), case["gate"], case["up"],
+                                     case["down"], case["w"][lo:hi].copy(),
+                                     case["idx"][lo:hi].copy(), activation=0,
+                                     moe_type=moe_type, dtype="f32")
+            scale = float(np.sqrt(np.mean(ref * ref)))
+            worst = max(worst, float(np.abs(out.numpy() - ref).max()) / scale)
         stats = {k_: int(v) for k_, v in layer.last_stats.items()}
-        scale = float(np.sqrt(np.mean(ref * ref)))
-        result_q.put((rank, float(np.abs(out.numpy() - ref).max()) / scale, stats))
+        layer.close()
+        result_q.put((rank, worst, stats))
     finally:
         dist.destroy_process_group()
 
 
-def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="exact"):
+def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="exact",
+             transport="auto"):
     import candle_moe
     import expert_parallel
     from moe_testlib import to_torch
@@ -170,10 +272,11 @@ def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="
         D = None if case["down"] is None else to_torch(case["down"], dtype)
         w = torch.from_numpy(case["w"]).cuda()
         idx = torch.from_numpy(case["idx"]).cuda()
-        layer = expert_parallel.ExpertParallelMoE(E, k, 0, mode=mode)
-        out = layer.forward(x[lo:hi].contiguous(), G[e0:e1].contiguous(), U[e0:e1].contiguous(),
-                            None if D is None else D[e0:e1].contiguous(), w[lo:hi].contiguous(),
-                            idx[lo:hi].contiguous(), moe_type)
+        layer = expert_parallel.ExpertParallelMoE(E, k, 0, mode=mode, transport=transport)
+        for _ in range(2):  # the second forward reuses the landing buffers and flag epochs
+            out = layer.forward(x[lo:hi].contiguous(), G[e0:e1].contiguous(),
+                                U[e0:e1].contiguous(), None if D is None else D[e0:e1].contiguous(),
+                                w[lo:hi].contiguous(), idx[lo:hi].contiguous(), moe_type)
         ref = candle_moe.FusedMoE(E, k).forward(x[lo:hi].contiguous(), G, U, D,
                                                 w[lo:hi].contiguous(), idx[lo:hi].contiguous(),
                                                 moe_type)
@@ -186,6 +289,8 @@ def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="
             same = bool(((o - r_).abs() <= 1e-2 * r_.abs() + 1e-2 * rms).all())
         diff = float((o - r_).abs().max()) / rms
         stats = {k_: int(v) for k_, v in layer.last_stats.items()}
-        result_q.put((rank, same, diff, stats))
+        stats["error_bits"] = candle_moe.device_error_bits(rank)
+        layer.close()
+        result_q.put((rank, same and stats["error_bits"] == 0, diff, stats))
     finally:
         dist.destroy_process_group()

@@ -1,31 +1,85 @@
-"""Expert-parallel exchange logic on two CPU ranks (gloo): bucketing by destination rank,
-all_to_all_single of counts / rows / metadata, the return trip and the slot-ordered combine,
-with the oracle standing in for the GPU compute.  Exact mode must equal the single-process oracle
-bit for bit (every contribution computed alone, summed in the same slot order); partials mode
-sums each rank's slots before the ranks are summed, so it agrees up to f32 reassociation."""
-import multiprocessing as pymp
-
+"""Expert-parallel exchange logic on two CPU ranks (gloo): bucketing by destination rank, the
+counts exchange, dispatch of rows and metadata, the return trip and the slot-ordered combine,
+with the oracle standing in for the GPU compute.  Both transports run: "collective"
+(all_to_all_single) and "p2p" (landing buffers written directly by the senders, here host shared
+memory in place of peer-mapped HBM, with the same layout, arrival flags, epochs and collective
+growth as on GPUs).  Exact mode must equal the single-process oracle bit for bit (every
+contribution computed alone, summed in the same slot order); partials mode sums each rank's slots
+before the ranks are summed, so it agrees up to f32 reassociation."""
+import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
 import ep_worker
 
 
-@pytest.mark.parametrize("mode", ["exact", "partials"])
-@pytest.mark.parametrize("moe_type", [0, 1])
-def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode):
+def _run(moe_type, mode, transport, sizes=None, T=40):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = ep_worker.free_port()
     procs = [ctx.Process(target=ep_worker.cpu_rank,
-                         args=(r, 2, port, 40, 32, 48, 8, 3, moe_type, q, mode))
+                         args=(r, 2, port, T, 32, 48, 8, 3, moe_type, q, mode, transport, sizes))
              for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=240)
         assert p.exitcode == 0, p.exitcode
-    results = sorted(q.get() for _ in range(2))
-    for rank, maxdiff, stats in results:
+    return sorted(q.get() for _ in range(2))
+
+
+@pytest.mark.parametrize("transport", ["collective", "p2p"])
+@pytest.mark.parametrize("mode", ["exact", "partials"])
+@pytest.mark.parametrize("moe_type", [0, 1])
+def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode, transport):
+    for rank, maxdiff, stats in _run(moe_type, mode, transport):
         assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
         assert stats["pairs_sent"] > 0 and stats["rows_received"] > 0
+
+
+@pytest.mark.parametrize("mode", ["exact", "partials"])
+def test_p2p_landing_buffers_grow_and_epochs_continue(mode):
+    """Three forwards through one layer: 2 tokens per rank (fewer than the 3 chunks, so some
+    chunks are empty), then 40 (the landing buffers must grow on every rank), then 17 (reuse)."""
+    for rank, maxdiff, stats in _run(0, mode, "p2p", sizes=[2, 40, 17]):
+        assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
+        assert stats["landing_regrows"] == 2, stats
+
+
+def test_p2p_layout_places_blocks_like_all_to_all():
+    """p2p_layout: the landing rows of each rank hold, per chunk, the blocks of every source in
+    source order (what all_to_all_single delivers), and the returned rows land in the origin's
+    pair order."""
+    import expert_parallel
+    rng = np.random.default_rng(5)
+    G, C = 3, 4
+    allc = rng.integers(0, 5, size=(G, C, G, 3))
+    allc[..., 1] = allc[..., 0]
+    send_start, recv_start, back_start, y_start = expert_parallel.p2p_layout(allc)
+    pairs = allc[..., 0]
+    # send buffers: row id = (source, chunk, destination, index)
+    send = [[(s, c, d, i) for c in range(C) for d in range(G) for i in range(pairs[s, c, d])]
+            for s in range(G)]
+    land = [[None] * int(pairs[:, :, d].sum()) for d in range(G)]
+    for s in range(G):
+        for c in range(C):
+            for d in range(G):
+                n = pairs[s, c, d]
+                a, b = send_start[s, c, d], recv_start[d, c, s]
+                land[d][b:b + n] = send[s][a:a + n]
+    for d in range(G):
+        expect = [(s, c, d, i) for c in range(C) for s in range(G) for i in range(pairs[s, c, d])]
+        assert land[d] == expect
+    # return: rank d's chunk-c results are its chunk-c landing rows in order; they must land in
+    # the origin's return region in the origin's pair (send) order
+    back = [[None] * int(pairs[s].sum()) for s in range(G)]
+    for d in range(G):
+        for c in range(C):
+            r0 = recv_start[d, c, 0]
+            res = land[d][r0:r0 + int(pairs[:, c, d].sum())]
+            for s in range(G):
+                n = pairs[s, c, d]
+                a, b = y_start[d, c, s], back_start[s, c, d]
+                back[s][b:b + n] = res[a:a + n]
+    for s in range(G):
+        assert back[s] == send[s]

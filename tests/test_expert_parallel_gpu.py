@@ -1,6 +1,8 @@
-"""Expert-parallel config-5-shaped layer on 2 GPUs over NCCL vs the single-GPU fused path on the
-same tokens: exact mode bit-identical (every contribution computed and rounded as on one GPU,
-combined in the same slot order); partials mode within the bf16 tolerance (1e-2 relative)."""
+"""Expert-parallel config-5-shaped layer on 2 GPUs vs the single-GPU fused path on the same
+tokens, two forwards per layer, both transports (p2p landing buffers filled by copy engines; NCCL
+all_to_all): exact mode bit-identical (every contribution computed and rounded as on one GPU,
+combined in the same slot order); partials mode within the bf16 tolerance (1e-2 relative); no
+device error bits (no arrival wait ran out)."""
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -12,14 +14,16 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
 @pytest.mark.parametrize("mode", ["exact", "partials"])
 @pytest.mark.parametrize("moe_type", [0, 1])
-def test_expert_parallel_two_gpus(moe_type, mode):
+def test_expert_parallel_two_gpus(moe_type, mode, transport):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = ep_worker.free_port()
     procs = [ctx.Process(target=ep_worker.gpu_rank,
-                         args=(r, 2, port, 3000, 256, 256, 16, 8, moe_type, "bf16", q, mode))
+                         args=(r, 2, port, 3000, 256, 256, 16, 8, moe_type, "bf16", q, mode,
+                               transport))
              for r in range(2)]
     for p in procs:
         p.start()

@@ -32,6 +32,27 @@ def test_router_bit_exact_vs_reference(E, k):
     assert torch.equal(w.view(torch.int32), rw.view(torch.int32))  # bit-identical weights
 
 
+@pytest.mark.parametrize("E", [8, 128, 256])
+def test_router_ties_and_non_finite_rows_bit_exact_vs_reference(E):
+    """Logits from a 5-value set (ties on every row), plus rows with -inf, +inf and NaN logits:
+    the picks (value, then lowest expert) and their bits match the reference kernel, including the
+    rows whose probabilities are NaN."""
+    k = 8
+    g = torch.Generator().manual_seed(E)
+    x = torch.randint(-2, 3, (1500, E), generator=g).float()
+    x[7, 3] = float("-inf")
+    x[11, :E // 2] = float("-inf")
+    x[13, 5] = float("inf")
+    x[17, E - 1] = float("nan")
+    x = x.cuda()
+    rw, ri, rs = refkernels.topk_softmax(x, k)
+    w, i, s = candle_moe.topk_softmax(x, k)
+    torch.cuda.synchronize()
+    assert torch.equal(i, ri)
+    assert torch.equal(s, rs)
+    assert torch.equal(w.view(torch.int32), rw.view(torch.int32))
+
+
 @pytest.mark.parametrize("T,k,E", [(512, 2, 8), (4096, 8, 16), (8192, 8, 128), (3000, 2, 7)])
 def test_route_prep_vs_reference(T, k, E):
     rng = np.random.default_rng(T + k + E)
