@@ -346,7 +346,7 @@ def run_ours(args, world, rank, local):
         st, n = layer.stage_times()
         line["ep_stages_ms"] = {s_: v / max(n, 1) for s_, v in st.items()}
         line["ep_rows"] = {k_: int(v) for k_, v in layer.last_stats.items()}
-        if layer.transport == "p2p":
+        if layer.transport in ("push", "copy"):
             line["ep_timeline_ms"] = {k_: round(v, 3) for k_, v in layer.timeline().items()}
     if not router_only and ncalls:
         rows = layer.last_stats["assignments_received"] if ep else T * k
@@ -374,7 +374,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not router_only:
         line["cpu_baseline"] = cpu_baseline(cfg, inp, target_s=args.cpu_seconds)
     if ep:
-        # non-zero when an arrival wait of the p2p exchange ran out (a rank never signalled)
+        # non-zero when an arrival wait of the exchange ran out (a rank never signalled)
         line["device_error_bits"] = int(max_over_ranks(world,
                                                        candle_moe.device_error_bits(local)))
         layer.close()
@@ -481,9 +481,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-mode", choices=["partials", "exact"], default="partials",
                     help="expert-parallel return: per-rank partial sums or per-slot rows")
-    ap.add_argument("--ep-transport", choices=["p2p", "collective"], default="p2p",
-                    help="expert-parallel row exchange: copy engines into peer-mapped landing "
-                         "buffers, or NCCL all_to_all_single")
+    ap.add_argument("--ep-transport", choices=["push", "copy", "collective"], default="push",
+                    help="expert-parallel row exchange into peer-mapped landing buffers by SM "
+                         "stores fused with pack / slot sum (push) or by copy engines (copy), "
+                         "or NCCL all_to_all_single (collective)")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
     ap.add_argument("--tokens", type=int, default=0,

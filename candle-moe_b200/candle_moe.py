@@ -112,6 +112,13 @@ def lib() -> ctypes.CDLL:
         L.moe_peer_signal.restype = ctypes.c_int
         L.moe_peer_wait.argtypes = [P, I32, U32, I64, P]
         L.moe_peer_wait.restype = ctypes.c_int
+        PP = ctypes.POINTER(ctypes.c_void_p)
+        L.moe_ep_push_pairs.argtypes = [P, P, P, P, I32, P, P, I32, I32, I32, I32, U32, PP, PP,
+                                        P, I32, P]
+        L.moe_ep_push_pairs.restype = ctypes.c_int
+        L.moe_segment_sum_push.argtypes = [P, P, I64, I32, U32, I32, PP,
+                                           ctypes.POINTER(ctypes.c_int64), I32, P]
+        L.moe_segment_sum_push.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -662,3 +669,38 @@ class _RawDeviceMemory:
 def device_bytes(ptr: int, nbytes: int, device) -> torch.Tensor:
     """A uint8 tensor over memory this module allocated (the caller keeps it alive)."""
     return torch.as_tensor(_RawDeviceMemory(ptr, nbytes), device=device)
+
+
+def ep_push_pairs(x: torch.Tensor, pair_token: torch.Tensor, pair_flat: torch.Tensor,
+                  pair_offsets: torch.Tensor, chunk: int, expert_indices: torch.Tensor,
+                  routing_weights: torch.Tensor, num_experts: int, num_ranks: int, dst_rows,
+                  dst_meta, slot_count: Optional[torch.Tensor], stream: torch.cuda.Stream,
+                  blocks: int = 0) -> None:
+    """Dispatch of one chunk fused with the pack (see include/candle_moe.h): rows and metadata go
+    straight to the destinations' addresses dst_rows[d] / dst_meta[d] (ints)."""
+    T, k = expert_indices.shape
+    G = num_ranks
+    rows = (ctypes.c_void_p * G)(*dst_rows)
+    meta = (ctypes.c_void_p * G)(*dst_meta)
+    st = lib().moe_ep_push_pairs(_ptr(x), _ptr(pair_token), _ptr(pair_flat), _ptr(pair_offsets),
+                                 chunk, _ptr(expert_indices), _ptr(routing_weights), k,
+                                 num_experts, G, x.shape[1], fused_moe_internal_dtype(x.dtype),
+                                 rows, meta, _ptr(slot_count), blocks,
+                                 ctypes.c_void_p(stream.cuda_stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_ep_push_pairs")
+
+
+def segment_sum_push(rows_in: torch.Tensor, segment_start: torch.Tensor, dst, first_row,
+                     stream: torch.cuda.Stream, blocks: int = 0) -> None:
+    """segment_sum_rows whose output rows [first_row[s], first_row[s+1]) go to the address
+    dst[s] (ints) instead of a local tensor."""
+    G = len(dst)
+    R = segment_start.numel() - 1
+    d = (ctypes.c_void_p * G)(*dst)
+    f = (ctypes.c_int64 * (G + 1))(*first_row)
+    st = lib().moe_segment_sum_push(_ptr(rows_in), _ptr(segment_start), R, rows_in.shape[1],
+                                    fused_moe_internal_dtype(rows_in.dtype), G, d, f, blocks,
+                                    ctypes.c_void_p(stream.cuda_stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_segment_sum_push")

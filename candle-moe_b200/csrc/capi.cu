@@ -793,3 +793,65 @@ CMOE_API int moe_peer_wait(const uint32_t* flags, int32_t count, uint32_t value,
   return finish(MOE_OK);
 }
 
+
+CMOE_API int moe_ep_push_pairs(const void* input, const int32_t* pair_token,
+                               const int32_t* pair_flat, const int32_t* pair_offsets,
+                               int32_t chunk, const uint32_t* expert_indices,
+                               const float* routing_weights, int32_t topk, int32_t num_experts,
+                               int32_t num_ranks, int32_t hidden_dim, uint32_t dtype,
+                               void* const* dst_rows, void* const* dst_meta, int32_t* slot_count,
+                               int32_t blocks, void* stream) {
+  if (topk <= 0 || num_experts <= 0 || num_ranks <= 0 || num_ranks > kMaxEpRanks ||
+      hidden_dim <= 0 || dtype > 2 || chunk < 0 || blocks < 0)
+    return MOE_ERR_INVALID_ARG;
+  if (!input || !pair_token || !pair_flat || !pair_offsets || !expert_indices ||
+      !routing_weights || !dst_rows || !dst_meta)
+    return MOE_ERR_INVALID_ARG;
+  EpPeerRows tab{};
+  for (int d = 0; d < num_ranks; ++d) {
+    if (!dst_rows[d] || !dst_meta[d]) return MOE_ERR_INVALID_ARG;
+    tab.rows[d] = static_cast<char*>(dst_rows[d]);
+    tab.meta[d] = static_cast<char*>(dst_meta[d]);
+  }
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_ep_push_pairs(static_cast<int>(dtype), input, pair_token, pair_flat, pair_offsets,
+                           chunk, expert_indices, routing_weights, topk, num_experts, num_ranks,
+                           hidden_dim, tab, slot_count, blocks ? blocks : ds->num_sms,
+                           static_cast<cudaStream_t>(stream)))
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_segment_sum_push(const void* rows_in, const int64_t* segment_start,
+                                  int64_t num_segments, int32_t hidden_dim, uint32_t dtype,
+                                  int32_t num_ranks, void* const* dst, const int64_t* first_row,
+                                  int32_t blocks, void* stream) {
+  if (num_segments < 0 || hidden_dim <= 0 || dtype > 2 || num_ranks <= 0 ||
+      num_ranks > kMaxEpRanks || blocks < 0)
+    return MOE_ERR_INVALID_ARG;
+  if (num_segments == 0) return MOE_OK;
+  if (!rows_in || !segment_start || !dst || !first_row) return MOE_ERR_INVALID_ARG;
+  EpPeerReturn tab{};
+  for (int s = 0; s <= num_ranks; ++s) {
+    if (s < num_ranks) {
+      if (!dst[s]) return MOE_ERR_INVALID_ARG;
+      tab.dst[s] = static_cast<char*>(dst[s]);
+    }
+    if (first_row[s] < 0 || (s > 0 && first_row[s] < first_row[s - 1]))
+      return MOE_ERR_INVALID_ARG;
+    tab.first[s] = first_row[s];
+  }
+  if (tab.first[0] != 0 || tab.first[num_ranks] != num_segments) return MOE_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (launch_segment_sum_push(static_cast<int>(dtype), rows_in, segment_start, num_segments,
+                              hidden_dim, num_ranks, tab, blocks ? blocks : ds->num_sms,
+                              static_cast<cudaStream_t>(stream)))
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}

@@ -155,6 +155,103 @@ __global__ void __launch_bounds__(256) segment_sum_rows_kernel(const T* __restri
   }
 }
 
+// ---- fused exchange kernels: SM stores over NVLink into peer-mapped landing buffers ---------
+
+// Dispatch of chunk c, fused with the pack: pair r in [off[c*G], off[c*G+G]) (sorted by
+// destination d, then token) goes to row (r - off[c*G + d]) of the block that this rank owns in
+// d's landing buffer, tab.rows[d] (row bytes) and tab.meta[d] (2k ints).  One warp per pair;
+// count[r] = slots of the pair (exact mode's bookkeeping).  Ends with a system-scope fence so
+// the arrival flag stored after this kernel orders behind the rows.
+// 128 threads x at most 48 registers (launch bounds for 10 blocks): one block fits beside a
+// persistent GEMM CTA on every SM, so these kernels run while the GEMMs of another chunk do.
+template <typename V>
+__global__ void __launch_bounds__(128, 10) ep_push_pairs_kernel(
+    const V* __restrict__ x, const int32_t* __restrict__ pair_token,
+    const int32_t* __restrict__ pair_flat, const int32_t* __restrict__ off, int c,
+    const uint32_t* __restrict__ idx, const float* __restrict__ w, int k, int E, int El, int G,
+    int vec_per_row, const EpPeerRows tab, int32_t* __restrict__ count) {
+  const int lane = threadIdx.x & 31;
+  const int64_t p0 = __ldg(off + c * G), p1 = __ldg(off + c * G + G);
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  constexpr int kU = 4;  // 16-byte units in flight per lane
+  for (int64_t r = p0 + warp0; r < p1; r += nwarps) {
+    const int64_t t = __ldg(pair_token + r);
+    const int d = __ldg(pair_flat + r) % G;
+    const int64_t pos = r - __ldg(off + c * G + d);
+    const V* src = x + t * vec_per_row;
+    V* dst = reinterpret_cast<V*>(tab.rows[d]) + pos * vec_per_row;
+    for (int c0 = 0; c0 < vec_per_row; c0 += 32 * kU) {
+      V q[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int cc = c0 + u * 32 + lane;
+        if (cc < vec_per_row) q[u] = __ldg(src + cc);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int cc = c0 + u * 32 + lane;
+        if (cc < vec_per_row) dst[cc] = q[u];
+      }
+    }
+    if (lane < k) {
+      const uint32_t e = __ldg(idx + t * k + lane);
+      const bool mine = e < static_cast<uint32_t>(E) && static_cast<int>(e / El) == d;
+      int32_t* m = reinterpret_cast<int32_t*>(tab.meta[d]) + pos * 2 * k;
+      m[lane] = mine ? static_cast<int32_t>(e % El) : El;
+      m[k + lane] = mine ? __float_as_int(__ldg(w + t * k + lane)) : 0;
+      const uint32_t ballot = __ballot_sync(0xffffffffu >> (32 - k), mine);
+      if (lane == 0 && count) count[r] = __popc(ballot);
+    }
+  }
+  __threadfence_system();
+}
+
+// Return of chunk c, fused with the slot sum: output row r (received-row order, grouped by
+// origin s: rows [tab.first[s], tab.first[s+1])) = sum of rows_in[start[r] .. start[r+1]) in
+// order, f32 accumulation, one rounding, stored to tab.dst[s] + (r - tab.first[s]) rows.  One warp
+// per row, KC rows of a segment loaded at once.  Ends with a system-scope fence.
+template <typename T, int KC>
+__global__ void __launch_bounds__(128, 10) segment_sum_push_kernel(
+    const T* __restrict__ rows_in, const int64_t* __restrict__ start, int64_t R, int H, int G,
+    const EpPeerReturn tab) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int units = H / V;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const int s = __popc(__ballot_sync(0xffffffffu, lane < G && tab.first[lane] <= r)) - 1;
+    T* dst = reinterpret_cast<T*>(tab.dst[s]) + (r - tab.first[s]) * H;
+    const int64_t s0 = __ldg(start + r), s1 = __ldg(start + r + 1);
+    for (int u = lane; u < units; u += 32) {
+      float acc[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      for (int64_t b = s0; b < s1; b += KC) {
+        uint4 q[KC];
+#pragma unroll
+        for (int j = 0; j < KC; ++j)
+          q[j] = b + j < s1 ? __ldcs(reinterpret_cast<const uint4*>(rows_in + (b + j) * H) + u)
+                            : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int j = 0; j < KC; ++j) {
+          if (b + j >= s1) continue;
+          const T* qe = reinterpret_cast<const T*>(&q[j]);
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] += Elem<T>::to_f(qe[i]);
+        }
+      }
+      uint4 qo;
+      T* qe = reinterpret_cast<T*>(&qo);
+#pragma unroll
+      for (int i = 0; i < V; ++i) qe[i] = Elem<T>::from_f(acc[i]);
+      reinterpret_cast<uint4*>(dst)[u] = qo;
+    }
+  }
+  __threadfence_system();
+}
+
 static unsigned ep_grid(int64_t work, int num_sms) {
   int64_t b = (work + 255) / 256;
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
@@ -220,6 +317,39 @@ static void segment_sum_t(const void* in, const int64_t* start, int64_t R, int H
   else
     segment_sum_rows_kernel<T, 1, 4><<<ep_grid(R * H, num_sms), 256, 0, s>>>(
         static_cast<const T*>(in), start, R, H, static_cast<T*>(out));
+}
+
+int launch_ep_push_pairs(int dtype, const void* x, const int32_t* pair_token,
+                         const int32_t* pair_flat, const int32_t* off, int c,
+                         const uint32_t* idx, const float* w, int k, int E, int G, int H,
+                         const EpPeerRows& tab, int32_t* count, int blocks, cudaStream_t s) {
+  const size_t row_bytes = static_cast<size_t>(H) * (dtype == kF32 ? 4 : 2);
+  if (G < 1 || G > kMaxEpRanks || E % G != 0 || k > 32 || row_bytes % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(x) % 16 != 0 || blocks < 1)
+    return 1;
+  for (int d = 0; d < G; ++d)
+    if (reinterpret_cast<uintptr_t>(tab.rows[d]) % 16 != 0) return 1;
+  ep_push_pairs_kernel<uint4><<<blocks, 128, 0, s>>>(
+      static_cast<const uint4*>(x), pair_token, pair_flat, off, c, idx, w, k, E, E / G, G,
+      static_cast<int>(row_bytes / 16), tab, count);
+  return 0;
+}
+
+int launch_segment_sum_push(int dtype, const void* in, const int64_t* start, int64_t R, int H,
+                            int G, const EpPeerReturn& tab, int blocks, cudaStream_t s) {
+  if (R <= 0) return 0;
+  if (dtype == kF32 || H % 8 != 0 || G < 1 || G > kMaxEpRanks || blocks < 1 ||
+      reinterpret_cast<uintptr_t>(in) % 16 != 0)
+    return 1;
+  for (int d = 0; d < G; ++d)
+    if (reinterpret_cast<uintptr_t>(tab.dst[d]) % 16 != 0) return 1;
+  if (dtype == kBF16)
+    segment_sum_push_kernel<__nv_bfloat16, 4><<<blocks, 128, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(in), start, R, H, G, tab);
+  else
+    segment_sum_push_kernel<__half, 4><<<blocks, 128, 0, s>>>(static_cast<const __half*>(in),
+                                                             start, R, H, G, tab);
+  return 0;
 }
 
 int launch_segment_sum_rows(int dtype, const void* in, const int64_t* start, int64_t R, int H,

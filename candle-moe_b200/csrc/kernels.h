@@ -96,6 +96,23 @@ int launch_ep_entry_flat(const int32_t* pair_token, const int32_t* pair_flat,
                          const int64_t* start, int64_t U, const uint32_t* idx, int k, int E,
                          int G, int32_t* flat, int num_sms, cudaStream_t s);
 
+// fused exchange kernels (ep_kernels.cu): destinations in peer-mapped landing buffers
+constexpr int kMaxEpRanks = 32;
+struct EpPeerRows {
+  char* rows[kMaxEpRanks];  // per destination: first row of this rank's block
+  char* meta[kMaxEpRanks];
+};
+struct EpPeerReturn {
+  char* dst[kMaxEpRanks];             // per origin: first row of this rank's block
+  int64_t first[kMaxEpRanks + 1];     // output rows [first[s], first[s+1]) go to origin s
+};
+int launch_ep_push_pairs(int dtype, const void* x, const int32_t* pair_token,
+                         const int32_t* pair_flat, const int32_t* off, int c,
+                         const uint32_t* idx, const float* w, int k, int E, int G, int H,
+                         const EpPeerRows& tab, int32_t* count, int blocks, cudaStream_t s);
+int launch_segment_sum_push(int dtype, const void* in, const int64_t* start, int64_t R, int H,
+                            int G, const EpPeerReturn& tab, int blocks, cudaStream_t s);
+
 // arrival flags of the expert-parallel exchange (peer.cu)
 constexpr int kMaxPeerFlags = 64;
 struct PeerFlagPtrs {

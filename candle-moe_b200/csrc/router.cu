@@ -39,10 +39,12 @@ __device__ __forceinline__ float from_order_key(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-template <int E>
+// KC > 0: k is the compile-time KC (rounds unrolled, pick bookkeeping folded); KC = 0: any k.
+template <int E, int KC>
 __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
     const float* __restrict__ logits, float* __restrict__ out_w, int32_t* __restrict__ out_idx,
-    int32_t* __restrict__ out_src, int num_tokens, int k, int renorm) {
+    int32_t* __restrict__ out_src, int num_tokens, int k_arg, int renorm) {
+  const int k = KC > 0 ? KC : k_arg;
   using G = RouterGeom<E>;
   constexpr int kElts = G::kElts, kVpt = G::kVpt, kTpr = G::kTpr, kVecs = G::kVecs;
   const int lane = threadIdx.x & 31;
@@ -52,22 +54,31 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
   const int64_t warp0 = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
   const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * warps_per_block;
 
-  for (int64_t wbase = warp0 * G::kRpw; wbase < num_tokens; wbase += warp_stride * G::kRpw) {
-    const int64_t row = wbase + sub;
-    const bool active = row < num_tokens;
-    float v[kVpt];
-    if (active) {
+  // this lane's logits of `row` (zeros past the last row)
+  auto load_row = [&](int64_t row, float (&dst)[kVpt]) {
+    if (row < num_tokens) {
       const float* rp = logits + row * E + g * kElts;
 #pragma unroll
       for (int l = 0; l < kVecs; ++l) {
         const FVec<kElts> q = *reinterpret_cast<const FVec<kElts>*>(rp + l * kElts * kTpr);
 #pragma unroll
-        for (int i = 0; i < kElts; ++i) v[l * kElts + i] = q.v[i];
+        for (int i = 0; i < kElts; ++i) dst[l * kElts + i] = q.v[i];
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < kVpt; ++i) v[i] = 0.f;
+      for (int i = 0; i < kVpt; ++i) dst[i] = 0.f;
     }
+  };
+  const int64_t row_stride = warp_stride * G::kRpw;
+  float vn[kVpt];
+  load_row(warp0 * G::kRpw + sub, vn);
+  for (int64_t wbase = warp0 * G::kRpw; wbase < num_tokens; wbase += row_stride) {
+    const int64_t row = wbase + sub;
+    const bool active = row < num_tokens;
+    float v[kVpt];
+#pragma unroll
+    for (int i = 0; i < kVpt; ++i) v[i] = vn[i];
+    load_row(row + row_stride, vn);  // the next row's loads overlap this row's work
     // softmax (max subtracted), same operation order as the reference
     float m = v[0];
 #pragma unroll
@@ -100,29 +111,75 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
       pw[s2] = 0.f;
       pe[s2] = 0;
     }
-    // When one warp owns the row and its probabilities are numbers, each round is two warp
-    // reductions in hardware: the largest value (as an order-preserving 32-bit key), then the
-    // lowest expert holding it -- the same pick as the shuffle argmax, which rows with NaN
-    // probabilities keep (its picks there depend on the lane order, as in the reference).
-    const bool redux = kTpr == 32 && (__float_as_uint(s) & 0x7fffffffu) <= 0x7f800000u;
-    for (int j = 0; j < k; ++j) {
-      float best;
-      int be;
-      if (redux) {
-        uint32_t kl = 0;
+    // Records pick j: kept for the coalesced store, or written at once when not staged.
+    auto record = [&](int j, float best, int be) {
+      wsum += best;
+      if (staged) {
+        if (j % kTpr == g) {
 #pragma unroll
-        for (int i = 0; i < kVpt; ++i) kl = max(kl, order_key(v[i]));
-        const uint32_t km = __reduce_max_sync(0xffffffffu, kl);
-        uint32_t cand = 0xffffffffu;
+          for (int s2 = 0; s2 < kSlots; ++s2)
+            if (s2 == j / kTpr) {
+              pw[s2] = best;
+              pe[s2] = be;
+            }
+        }
+      } else if (active && g == 0) {
+        const int64_t o = row * k + j;
+        out_w[o] = best;
+        out_idx[o] = be;
+        out_src[o] = static_cast<int32_t>(static_cast<int64_t>(j) * num_tokens + row);
+      }
+    };
+    // When one warp owns the row, its probabilities are numbers and k <= E, the picks -- largest
+    // value first, ties to the lower expert -- come from each lane's values sorted once by
+    // (value desc, expert asc): a round is one warp max over the lanes' heads (as
+    // order-preserving 32-bit keys), one warp min over the experts of the lanes at that max, and
+    // the winning lane pops its head.  Same picks as the shuffle argmax below, which the other
+    // rows keep (with NaN its picks depend on the lane order, as in the reference; with k > E it
+    // re-picks cleared experts at -10000, as the reference does).
+    const bool redux = kTpr == 32 && k <= E && (__float_as_uint(s) & 0x7fffffffu) <= 0x7f800000u;
+    if (redux) {
+      uint32_t key[kVpt];
+      int id[kVpt];
 #pragma unroll
-        for (int i = kVpt - 1; i >= 0; --i)  // ascending expert ids: the first match is the lowest
-          if (order_key(v[i]) == km)
-            cand = static_cast<uint32_t>(col0 + (i / kElts) * kElts * kTpr + i % kElts);
-        be = static_cast<int>(__reduce_min_sync(0xffffffffu, cand));
-        best = from_order_key(km);
-      } else {
-        best = v[0];
-        be = col0;
+      for (int i = 0; i < kVpt; ++i) {
+        key[i] = order_key(v[i]);
+        id[i] = col0 + (i / kElts) * kElts * kTpr + i % kElts;
+      }
+      // odd-even transposition sort, kVpt rounds (a lane holds 4 or 8 values)
+#pragma unroll
+      for (int r = 0; r < kVpt; ++r) {
+#pragma unroll
+        for (int a = r & 1; a + 1 < kVpt; a += 2) {
+          const bool sw = key[a + 1] > key[a] || (key[a + 1] == key[a] && id[a + 1] < id[a]);
+          const uint32_t ka = key[a], kb = key[a + 1];
+          const int ia = id[a], ib = id[a + 1];
+          key[a] = sw ? kb : ka;
+          key[a + 1] = sw ? ka : kb;
+          id[a] = sw ? ib : ia;
+          id[a + 1] = sw ? ia : ib;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < (KC > 0 ? KC : k); ++j) {
+        const uint32_t km = __reduce_max_sync(0xffffffffu, key[0]);
+        const int be = static_cast<int>(
+            __reduce_min_sync(0xffffffffu, key[0] == km ? static_cast<uint32_t>(id[0]) : 0xffffffffu));
+        if (id[0] == be) {  // this lane held the pick: pop it (0 sorts below every value)
+#pragma unroll
+          for (int i = 0; i + 1 < kVpt; ++i) {
+            key[i] = key[i + 1];
+            id[i] = id[i + 1];
+          }
+          key[kVpt - 1] = 0u;
+          id[kVpt - 1] = 0x7fffffff;
+        }
+        record(j, from_order_key(km), be);
+      }
+    } else {
+      for (int j = 0; j < k; ++j) {
+        float best = v[0];
+        int be = col0;
 #pragma unroll
         for (int l = 0; l < kVecs; ++l) {
 #pragma unroll
@@ -143,32 +200,17 @@ __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
             be = oe;
           }
         }
-      }
-      wsum += best;
-      if (staged) {
-        if (j % kTpr == g) {
+        record(j, best, be);
+        // the owning lane clears the winner
+        if (g == (be / kElts) % kTpr) {
+          const int l = be / (kElts * kTpr);
+          const int i = be % kElts;
 #pragma unroll
-          for (int s2 = 0; s2 < kSlots; ++s2)
-            if (s2 == j / kTpr) {
-              pw[s2] = best;
-              pe[s2] = be;
-            }
+          for (int ll = 0; ll < kVecs; ++ll)
+#pragma unroll
+            for (int ii = 0; ii < kElts; ++ii)
+              if (ll == l && ii == i) v[ll * kElts + ii] = -10000.f;
         }
-      } else if (active && g == 0) {
-        const int64_t o = row * k + j;
-        out_w[o] = best;
-        out_idx[o] = be;
-        out_src[o] = static_cast<int32_t>(static_cast<int64_t>(j) * num_tokens + row);
-      }
-      // the owning lane clears the winner
-      if (g == (be / kElts) % kTpr) {
-        const int l = be / (kElts * kTpr);
-        const int i = be % kElts;
-#pragma unroll
-        for (int ll = 0; ll < kVecs; ++ll)
-#pragma unroll
-          for (int ii = 0; ii < kElts; ++ii)
-            if (ll == l && ii == i) v[ll * kElts + ii] = -10000.f;
       }
     }
     if (staged) {
@@ -195,17 +237,34 @@ int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int
                   int num_tokens, int k, int renorm, int num_sms, cudaStream_t stream) {
   if (num_tokens <= 0) return 0;
   const int threads = 256;
-  auto grid_for = [&](int rows_per_warp) {
+  // one wave: as many blocks as fit on the SMs at once (the grid-stride loop prefetches rows)
+  auto grid_for = [&](int rows_per_warp, int resident_per_sm) {
     const int64_t warps = (static_cast<int64_t>(num_tokens) + rows_per_warp - 1) / rows_per_warp;
     int64_t blocks = (warps + 7) / 8;
-    const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+    const int64_t cap = static_cast<int64_t>(num_sms) * resident_per_sm;
     return static_cast<int>(blocks < cap ? blocks : cap);
   };
+#define CMOE_ROUTER_LAUNCH(EE, KK)                                                              \
+  {                                                                                           \
+    static int resident = 0;                                                                  \
+    if (resident == 0) {                                                                      \
+      int r = 0;                                                                              \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(                                      \
+              &r, router_topk_softmax_kernel<EE, KK>, threads, 0) != cudaSuccess ||          \
+          r < 1)                                                                              \
+        r = 4;                                                                                \
+      resident = r;                                                                           \
+    }                                                                                         \
+    router_topk_softmax_kernel<EE, KK>                                                        \
+        <<<grid_for(RouterGeom<EE>::kRpw, resident), threads, 0, stream>>>(                   \
+            logits, w, idx, src, num_tokens, k, renorm);                                      \
+    return 0;                                                                                 \
+  }
 #define CMOE_ROUTER_CASE(EE)                                                                    \
   case EE:                                                                                    \
-    router_topk_softmax_kernel<EE><<<grid_for(RouterGeom<EE>::kRpw), threads, 0, stream>>>(   \
-        logits, w, idx, src, num_tokens, k, renorm);                                          \
-    return 0;
+    if (k == 2) CMOE_ROUTER_LAUNCH(EE, 2)                                                     \
+    if (k == 8) CMOE_ROUTER_LAUNCH(EE, 8)                                                     \
+    CMOE_ROUTER_LAUNCH(EE, 0)
   switch (num_experts) {
     CMOE_ROUTER_CASE(1)
     CMOE_ROUTER_CASE(2)
@@ -219,6 +278,7 @@ int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int
     default:
       return 1;
   }
+#undef CMOE_ROUTER_LAUNCH
 #undef CMOE_ROUTER_CASE
 }
 

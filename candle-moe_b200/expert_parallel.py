@@ -20,18 +20,24 @@ for.  With G ranks, rank r owns experts [r*E/G, (r+1)*E/G) and its own tokens.  
         single-GPU path;
  5. combine on the origin (moe_combine_rows), f32 accumulation, one rounding.
 
-Two transports move the rows of steps 3-4:
+Three transports move the rows of steps 3-4.  The first two share one landing buffer per rank
+(arrival flags, received rows and metadata, returned rows), allocated with moe_peer_alloc and
+mapped by every other rank; every offset follows from the all-gathered count matrix
+(p2p_layout), so each rank computes the same layout, and buffers grow collectively when a rank's
+need exceeds its capacity.  After a chunk's rows are in place the sender release-stores the
+chunk's epoch into the destination's flag for this sender (moe_peer_signal); the destination's
+compute stream waits for all senders' flags with a bounded wait (moe_peer_wait) before its GEMMs
+read the rows.
 
-  "p2p" (default on GPUs): every rank owns one landing buffer (arrival flags, received rows and
-    metadata, returned rows) allocated with moe_peer_alloc and mapped by every other rank.  A
-    sender copies each (chunk, destination) block straight to its final place in the
-    destination's landing buffer with the copy engines (moe_copy_async, one stream per peer), so
-    the transfer takes no SM time from the grouped GEMMs, then release-stores the chunk's epoch
-    into the destination's flag for this sender (moe_peer_signal); the destination's compute
-    stream waits for all senders' flags with a bounded wait (moe_peer_wait) before its GEMMs read
-    the rows.  Every offset follows from the all-gathered count matrix (p2p_layout), so each
-    rank computes the same layout; buffers grow collectively when a rank's need exceeds its
-    capacity.
+  "push" (default on GPUs): SM stores over NVLink, fused with the kernels that produce the rows:
+    moe_ep_push_pairs writes each pair's token row and metadata straight into the destination's
+    landing rows (no send buffer; chunks after the first on a side stream with one small block
+    per SM, beside the persistent GEMMs), and for the last chunk moe_segment_sum_push writes each
+    partial straight into the origin's return rows.  Earlier chunks' partials return by copy
+    engine (a slot sum beside the GEMMs would stream its rows through L2 and slow them).
+  "copy": a send buffer (moe_ep_pack) and copy-engine copies (moe_copy_async, one stream per
+    peer) into the same landing buffers; the copy engines take no SM time but move ~500 GB/s per
+    GPU at most in this all-to-all pattern.
   "collective": all_to_all_single on the process group's backend (NCCL; gloo on CPU), async on
     the backend's stream, with `sm_reserve` SMs left free by the persistent GEMMs.
 
@@ -101,7 +107,7 @@ class CudaOps:
     def set_sm_reserve(sms):
         return candle_moe.set_sm_reserve(sms)
 
-    # ---- p2p transport ----
+    # ---- landing-buffer transports ----
     peer_alloc = staticmethod(candle_moe.peer_alloc)
     peer_free = staticmethod(candle_moe.peer_free)
     peer_open = staticmethod(candle_moe.peer_open)
@@ -129,6 +135,20 @@ class CudaOps:
         return host.numpy()
 
     @staticmethod
+    def push_pairs(x, pair_token, pair_flat, off, chunk, idx, w, num_experts, num_ranks, rows_to,
+                   meta_to, stream, blocks):
+        candle_moe.ep_push_pairs(x, pair_token, pair_flat, off, chunk, idx, w, num_experts,
+                                 num_ranks, rows_to, meta_to, None, stream, blocks)
+
+    @staticmethod
+    def segment_sum_push(rows, start, dst, first, stream, blocks):
+        candle_moe.segment_sum_push(rows, start, dst, first, stream, blocks)
+
+    @staticmethod
+    def num_sms(device):
+        return torch.cuda.get_device_properties(device).multi_processor_count
+
+    @staticmethod
     def new_stream(device):
         return torch.cuda.Stream(device)
 
@@ -148,7 +168,7 @@ class CudaOps:
 
 
 def p2p_layout(allc: np.ndarray):
-    """Row offsets of the p2p exchange from the all-gathered counts.
+    """Row offsets of the landing-buffer exchange from the all-gathered counts.
 
     allc[s, c, d] = (pairs, returned rows, assignments) that rank s sends rank d in chunk c.
     Returns exclusive prefix sums (rows):
@@ -174,7 +194,7 @@ def _align(v: int, a: int = 256) -> int:
 
 
 class _Landing:
-    """The p2p landing buffers of all ranks: this rank's own (allocated) and every peer's
+    """The landing buffers of all ranks: this rank's own (allocated) and every peer's
     (mapped), with their capacities, and the epoch counters of the arrival flags.
 
     Buffer of rank r: [flags: 2G u32 | rows: cap_rows x row_bytes | meta: cap_rows x meta_bytes |
@@ -274,14 +294,14 @@ class ExpertParallelMoE:
         # SMs the expert GEMMs leave to NCCL's kernels while the collective exchange is in
         # flight: the GEMMs are persistent (one CTA per SM), and without free SMs the collectives
         # would only run between GEMM launches.  The GEMMs take tiles dynamically, so the reserve
-        # only costs the SMs themselves.  The p2p transport needs none.
+        # only costs the SMs themselves.  The landing-buffer transports need none.
         self.sm_reserve = sm_reserve
         if mode not in ("partials", "exact"):
             raise ValueError(f"unknown mode {mode!r}")
         self.mode = mode
         if transport == "auto":
-            transport = "p2p" if isinstance(self.ops, CudaOps) else "collective"
-        if transport not in ("p2p", "collective"):
+            transport = "push" if isinstance(self.ops, CudaOps) else "collective"
+        if transport not in ("push", "copy", "collective"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         self.wait_timeout_s = wait_timeout_s
@@ -302,7 +322,8 @@ class ExpertParallelMoE:
 
     def _point(self, name, stream=None):
         """Timeline point of the current timed forward (an event on `stream`, default the
-        current one); the p2p transport marks when each chunk's rows landed and were used."""
+        current one); the landing-buffer transports mark when each chunk's rows landed and were
+        used."""
         if self.timing:
             e = torch.cuda.Event(enable_timing=True)
             if stream is None:
@@ -332,7 +353,7 @@ class ExpertParallelMoE:
         return tot, len(self._events) // n
 
     def close(self):
-        """Collective: unmap and free the p2p landing buffers."""
+        """Collective: unmap and free the landing buffers."""
         if self._landing is not None:
             self._landing.release()
             self._landing = None
@@ -355,7 +376,7 @@ class ExpertParallelMoE:
         # us, and in exact mode also the rows that come back
         exact = self.mode == "exact"
         counts = torch.stack([pair_counts, asg if exact else pair_counts, asg], dim=2)
-        return idx, w, p_tok, p_flat, counts, off[C * G:C * G + 1]
+        return idx, w, p_tok, p_flat, counts, off
 
     def _local_experts(self, rx, rm):
         """Slot metadata of received rows: (local expert ids [R,k], weights [R,k], valid slots,
@@ -372,9 +393,9 @@ class ExpertParallelMoE:
                 expert_indices: torch.Tensor, moe_type: int) -> torch.Tensor:
         """x [T,H] local tokens; *_local: this rank's experts (gate/up [E/G,H,I], down [E/G,I,H]);
         routing_weights / expert_indices [T,k] with global expert ids.  Returns [T,H]."""
-        if self.transport == "p2p":
-            return self._forward_p2p(x, gate_local, up_local, down_local, routing_weights,
-                                     expert_indices, moe_type)
+        if self.transport in ("push", "copy"):
+            return self._forward_landing(x, gate_local, up_local, down_local, routing_weights,
+                                         expert_indices, moe_type)
         return self._forward_collective(x, gate_local, up_local, down_local, routing_weights,
                                         expert_indices, moe_type)
 
@@ -383,29 +404,31 @@ class ExpertParallelMoE:
         Tc = max(1, (T + C - 1) // C)
         return C, Tc
 
-    # ---- p2p transport -------------------------------------------------------------------------
-    def _forward_p2p(self, x, gate_local, up_local, down_local, routing_weights, expert_indices,
-                     moe_type):
+    # ---- landing-buffer transports ("push": SM stores over NVLink, "copy": copy engines) ------
+    def _forward_landing(self, x, gate_local, up_local, down_local, routing_weights,
+                         expert_indices, moe_type):
         T, H = x.shape
         k, G, E, El, me = self.k, self.world, self.num_experts, self.num_local, self.rank
         C, Tc = self._chunking(T)
         dev = x.device
         ops = self.ops
         exact = self.mode == "exact"
+        push = self.transport == "push"
         self._mark()
         if self.timing:
             self._timeline.append((self._events[-1], []))
 
         # 1-2. plan; the one host synchronisation: every rank's counts
-        idx, w, p_tok, p_flat, counts, n_dev = self._plan(x, routing_weights, expert_indices, C,
-                                                          Tc)
+        idx, w, p_tok, p_flat, counts, off = self._plan(x, routing_weights, expert_indices, C, Tc)
         self._point("planned")
         gathered = [torch.empty_like(counts) for _ in range(G)]
         work = dist.all_gather(gathered, counts, group=self.group, async_op=True)
-        # pack while the counts travel: the pair count is read on the device, the buffers hold
-        # every (token, rank) entry
-        send_x, meta, slot_count = ops.pack(x, p_tok, p_flat, idx, w, E, G, n_dev)
-        self._point("packed")
+        if not push:
+            # pack while the counts travel: the pair count is read on the device, the buffers
+            # hold every (token, rank) entry
+            send_x, meta, slot_count = ops.pack(x, p_tok, p_flat, idx, w, E, G,
+                                                off[C * G:C * G + 1])
+            self._point("packed")
         allc = ops.host_counts(work, gathered)               # [G_src, C, G_dst, 3]
         send_start, recv_start, back_start, y_start = p2p_layout(allc)
         pairs, back = allc[..., 0], allc[..., 1]
@@ -421,41 +444,62 @@ class ExpertParallelMoE:
         regions = [L.regions(r) for r in range(G)]
         copy_s, sig_s = self._streams[:G], self._streams[G]
         compute = ops.current_stream(dev)
+        sms = ops.num_sms(dev)
 
         p_tok, p_flat = p_tok[:U], p_flat[:U]
         if exact:
+            if push:  # the slots of each pair: its token's experts on the pair's rank
+                e = idx.long()[p_tok.long()] & 0xFFFFFFFF
+                d = (p_flat.long() % G)[:, None]
+                slot_count = ((e < E) & (torch.div(e, El, rounding_mode="floor") == d)).sum(1)
             sc = slot_count[:U].long()
             start = torch.cumsum(sc, 0) - sc
             back_flat = ops.entry_flat(p_tok, p_flat, start.contiguous(), idx, E, G, n_back)
         self._mark()
 
-        # 3. dispatch every chunk: copy engines, one stream per destination, then the flags
-        ev_pack = ops.record(compute)
-        for s in copy_s:
-            ops.wait(s, ev_pack)
-        self._point("copies_start", copy_s[(me + 1) % G])
-        x_addr, m_addr = send_x.data_ptr(), meta.data_ptr()
+        # 3. dispatch every chunk, then its arrival flag at every destination
         flag_d = [L.addr[r] + 4 * me for r in range(G)]
         flag_r = [L.addr[r] + 4 * (G + me) for r in range(G)]
         ep_d, ep_r = L.epoch_dispatch, L.epoch_return
-        for c in range(C):
-            for j in range(G):
-                d = (me + j) % G  # start with the next rank so senders spread over destinations
-                n = int(pairs[me, c, d])
-                if n:
-                    rows0, meta0 = regions[d][0], regions[d][1]
-                    r0 = int(recv_start[d, c, me])
-                    s0 = int(send_start[me, c, d])
-                    ops.copy_async(L.addr[d] + rows0 + r0 * row_b, x_addr + s0 * row_b,
-                                   n * row_b, copy_s[d])
-                    ops.copy_async(L.addr[d] + meta0 + r0 * meta_b, m_addr + s0 * meta_b,
-                                   n * meta_b, copy_s[d])
+        ev_ready = ops.record(compute)
+        if push:
+            # fused pack + dispatch: SM stores straight into the destinations' landing rows; the
+            # first chunk has the GPU to itself, later ones share it with the GEMMs
+            ops.wait(sig_s, ev_ready)
+            self._point("copies_start", sig_s)
+            for c in range(C):
+                rows_to = [L.addr[d] + regions[d][0] + int(recv_start[d, c, me]) * row_b
+                           for d in range(G)]
+                meta_to = [L.addr[d] + regions[d][1] + int(recv_start[d, c, me]) * meta_b
+                           for d in range(G)]
+                if int(pairs[me, c].sum()):
+                    ops.push_pairs(x, p_tok, p_flat, off, c, idx, w, E, G, rows_to, meta_to,
+                                   sig_s, 4 * sms if c == 0 else sms)
+                ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
+                self._point(f"sent{c}", sig_s)
+        else:
+            # copy engines, one stream per destination
             for s in copy_s:
-                ops.wait(sig_s, ops.record(s))
-            ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
-            self._point(f"sent{c}", sig_s)
+                ops.wait(s, ev_ready)
+            self._point("copies_start", copy_s[(me + 1) % G])
+            x_addr, m_addr = send_x.data_ptr(), meta.data_ptr()
+            for c in range(C):
+                for j in range(G):
+                    d = (me + j) % G  # start with the next rank: senders spread over destinations
+                    n = int(pairs[me, c, d])
+                    if n:
+                        r0 = int(recv_start[d, c, me])
+                        s0 = int(send_start[me, c, d])
+                        ops.copy_async(L.addr[d] + regions[d][0] + r0 * row_b,
+                                       x_addr + s0 * row_b, n * row_b, copy_s[d])
+                        ops.copy_async(L.addr[d] + regions[d][1] + r0 * meta_b,
+                                       m_addr + s0 * meta_b, n * meta_b, copy_s[d])
+                for s in copy_s:
+                    ops.wait(sig_s, ops.record(s))
+                ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
+                self._point(f"sent{c}", sig_s)
 
-        # 4. per chunk: wait for the rows, run the local experts, copy results back
+        # 4. per chunk: wait for the rows, run the local experts, send the results back
         keep = []
         received = computed = 0
         rows0, meta0, back0, _ = regions[me]
@@ -478,25 +522,37 @@ class ExpertParallelMoE:
             if n_asg:
                 ops.local_experts_scatter(rx, gate_local, up_local, down_local, w_loc, e_loc,
                                           out_row, contrib, El, self.activation, moe_type)
+            # segments of the results: a received row's consecutive contributions (partials),
+            # or each contribution alone (exact)
             if exact:
-                y = contrib
+                seg = torch.arange(n_asg + 1, dtype=torch.int64, device=dev)
             else:
-                # partial of each received row: its consecutive contributions, in slot order
-                start = torch.zeros((R + 1,), dtype=torch.int64, device=dev)
-                torch.cumsum(valid.sum(dim=1), 0, out=start[1:])
-                y = ops.segment_sum(contrib, start).to(x.dtype).contiguous()
+                seg = torch.zeros((R + 1,), dtype=torch.int64, device=dev)
+                torch.cumsum(valid.sum(dim=1), 0, out=seg[1:])
+            dst = [L.addr[s] + regions[s][2] + int(back_start[s, c, me]) * row_b
+                   for s in range(G)]
+            first = [int(v) for v in y_start[me, c]] + [n_out]
+            if push and c == C - 1:
+                # the last chunk has the GPU to itself: slot sum fused with the return, the
+                # partials stored straight into the origins' buffers.  (Earlier chunks sum on
+                # this stream and return by copy engine: a slot sum beside the next chunk's GEMMs
+                # streams its rows through L2 and slows them more than it saves.)
+                keep += [contrib, seg]
+                ops.segment_sum_push(contrib, seg, dst, first, compute, 4 * sms)
+                self._point(f"computed{c}")
+                continue
+            y = contrib if exact else ops.segment_sum(contrib, seg).to(x.dtype).contiguous()
             keep.append(y)
             self._point(f"computed{c}")
             ev_y = ops.record(compute)
             y_addr = y.data_ptr()
             for j in range(G):
                 s = (me + j) % G
-                n = int(back[s, c, me])
+                n = first[s + 1] - first[s]
                 if n:
                     ops.wait(copy_s[s], ev_y)
-                    ops.copy_async(L.addr[s] + regions[s][2] + int(back_start[s, c, me]) * row_b,
-                                   y_addr + int(y_start[me, c, s]) * row_b, n * row_b, copy_s[s])
-        for s in copy_s:
+                    ops.copy_async(dst[s], y_addr + first[s] * row_b, n * row_b, copy_s[s])
+        for s in copy_s + [compute]:
             ops.wait(sig_s, ops.record(s))
         ops.peer_signal(flag_r, ep_r + 1, sig_s)
         self._point("returned", sig_s)
@@ -511,8 +567,8 @@ class ExpertParallelMoE:
             out = ops.combine_rows(back_rows, back_flat, T, k)
         else:
             out = ops.combine_rows(back_rows, p_flat.contiguous(), T, G)
-        # the copy streams read send_x, meta and the results in `keep`: join them before those
-        # tensors can be freed, and before the next forward packs again
+        # the side streams read tensors of this forward (send buffers, results): join them before
+        # those tensors can be freed, and before the next forward writes again
         for s in self._streams:
             ops.wait(compute, ops.record(s))
         del keep

@@ -279,6 +279,36 @@ int moe_route_prep_noalloc(const uint32_t* expert_indices, const float* routing_
  *   (flag - value >= 0 as int32); after timeout_ns it sets bit 64 of the device error word
  *   (moe_device_error_bits) and lets the stream continue.
  */
+/*
+ * The same exchange with the rows moved by SM stores over NVLink, fused with the kernels that
+ * produce them (no staging buffer, no copy engine), for num_ranks <= 32:
+ *
+ * moe_ep_push_pairs: dispatch of chunk `chunk`, fused with moe_ep_pack: the pairs
+ *   [pair_offsets[chunk*num_ranks], pair_offsets[(chunk+1)*num_ranks]) (moe_route_prep_ex
+ *   offsets over the moe_ep_dest_groups groups, read on the device) are written to
+ *   dst_rows[d] + i rows and dst_meta[d] + i metadata rows (2*topk int32: local expert ids, then
+ *   weight bits, as moe_ep_pack) for the i-th pair of destination d; slot_count (optional) as
+ *   moe_ep_pack.  dst_rows / dst_meta: num_ranks device addresses, 16-byte aligned, usually in
+ *   peers' moe_peer_alloc buffers.
+ * moe_segment_sum_push: moe_segment_sum_rows whose output row r goes to
+ *   dst[s] + (r - first_row[s]) rows for first_row[s] <= r < first_row[s+1]
+ *   (first_row: num_ranks + 1 ascending offsets from 0 to num_segments); f16/bf16 only,
+ *   hidden_dim a multiple of 8.
+ * Both end with a system-scope fence, so a moe_peer_signal enqueued after them on the same
+ * stream publishes their rows.  blocks = 0: one 128-thread block per SM (each fits beside a
+ * persistent GEMM block).
+ */
+int moe_ep_push_pairs(const void* input, const int32_t* pair_token, const int32_t* pair_flat,
+                      const int32_t* pair_offsets, int32_t chunk, const uint32_t* expert_indices,
+                      const float* routing_weights, int32_t topk, int32_t num_experts,
+                      int32_t num_ranks, int32_t hidden_dim, uint32_t dtype,
+                      void* const* dst_rows, void* const* dst_meta, int32_t* slot_count,
+                      int32_t blocks, void* stream);
+int moe_segment_sum_push(const void* rows_in, const int64_t* segment_start, int64_t num_segments,
+                         int32_t hidden_dim, uint32_t dtype, int32_t num_ranks,
+                         void* const* dst, const int64_t* first_row, int32_t blocks,
+                         void* stream);
+
 #define MOE_PEER_HANDLE_BYTES 64
 int moe_peer_alloc(size_t bytes, void** ptr, uint8_t* handle);
 int moe_peer_free(void* ptr);

@@ -113,7 +113,7 @@ class CpuOracleOps:
     def set_sm_reserve(sms):
         return 0
 
-    # ---- p2p transport over host shared memory: each landing buffer is a file in /dev/shm that
+    # ---- landing buffers in host shared memory: each landing buffer is a file in /dev/shm that
     # every rank maps; copies are memmoves, flags 32-bit stores and polls (x86 keeps the order)
     _maps = {}
 
@@ -176,6 +176,31 @@ class CpuOracleOps:
                 if time.monotonic() - t0 > timeout_s:
                     raise TimeoutError(f"flag {i} never reached {value}")
                 time.sleep(0.0002)
+
+    @classmethod
+    def push_pairs(cls, x, pair_token, pair_flat, off, chunk, idx, w, num_experts, num_ranks,
+                   rows_to, meta_to, stream, blocks):
+        G = num_ranks
+        p0, p1 = int(off[chunk * G]), int(off[chunk * G + G])
+        rows, meta, _ = cls.pack(x, pair_token[p0:p1], pair_flat[p0:p1], idx, w, num_experts, G)
+        rb, mb = rows.shape[1] * rows.element_size(), meta.shape[1] * 4
+        for i in range(p1 - p0):
+            d = int(pair_flat[p0 + i]) % G
+            pos = p0 + i - int(off[chunk * G + d])
+            ctypes.memmove(rows_to[d] + pos * rb, rows[i].data_ptr(), rb)
+            ctypes.memmove(meta_to[d] + pos * mb, meta[i].data_ptr(), mb)
+
+    @classmethod
+    def segment_sum_push(cls, rows, start, dst, first, stream, blocks):
+        y = cls.segment_sum(rows, start).to(rows.dtype).contiguous()
+        rb = y.shape[1] * y.element_size()
+        for s in range(len(dst)):
+            for r in range(first[s], first[s + 1]):
+                ctypes.memmove(dst[s] + (r - first[s]) * rb, y[r].data_ptr(), rb)
+
+    @staticmethod
+    def num_sms(device):
+        return 1
 
     @staticmethod
     def host_counts(work, gathered):

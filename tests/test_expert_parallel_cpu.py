@@ -1,7 +1,8 @@
 """Expert-parallel exchange logic on two CPU ranks (gloo): bucketing by destination rank, the
 counts exchange, dispatch of rows and metadata, the return trip and the slot-ordered combine,
-with the oracle standing in for the GPU compute.  Both transports run: "collective"
-(all_to_all_single) and "p2p" (landing buffers written directly by the senders, here host shared
+with the oracle standing in for the GPU compute.  All transports run: "collective"
+(all_to_all_single), "copy" and "push" (landing buffers written directly by the senders -- a send
+buffer and block copies, or rows stored by the fused pack / slot-sum steps -- here host shared
 memory in place of peer-mapped HBM, with the same layout, arrival flags, epochs and collective
 growth as on GPUs).  Exact mode must equal the single-process oracle bit for bit (every
 contribution computed alone, summed in the same slot order); partials mode sums each rank's slots
@@ -28,7 +29,7 @@ def _run(moe_type, mode, transport, sizes=None, T=40):
     return sorted(q.get() for _ in range(2))
 
 
-@pytest.mark.parametrize("transport", ["collective", "p2p"])
+@pytest.mark.parametrize("transport", ["collective", "copy", "push"])
 @pytest.mark.parametrize("mode", ["exact", "partials"])
 @pytest.mark.parametrize("moe_type", [0, 1])
 def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode, transport):
@@ -37,11 +38,12 @@ def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode, transpor
         assert stats["pairs_sent"] > 0 and stats["rows_received"] > 0
 
 
+@pytest.mark.parametrize("transport", ["copy", "push"])
 @pytest.mark.parametrize("mode", ["exact", "partials"])
-def test_p2p_landing_buffers_grow_and_epochs_continue(mode):
+def test_landing_buffers_grow_and_epochs_continue(mode, transport):
     """Three forwards through one layer: 2 tokens per rank (fewer than the 3 chunks, so some
     chunks are empty), then 40 (the landing buffers must grow on every rank), then 17 (reuse)."""
-    for rank, maxdiff, stats in _run(0, mode, "p2p", sizes=[2, 40, 17]):
+    for rank, maxdiff, stats in _run(0, mode, transport, sizes=[2, 40, 17]):
         assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
         assert stats["landing_regrows"] == 2, stats
 

@@ -1,6 +1,6 @@
 """Expert-parallel config-5-shaped layer on 2 GPUs vs the single-GPU fused path on the same
-tokens, two forwards per layer, both transports (p2p landing buffers filled by copy engines; NCCL
-all_to_all): exact mode bit-identical (every contribution computed and rounded as on one GPU,
+tokens, two forwards per layer, all transports (landing buffers filled by the fused push kernels
+or by copy engines; NCCL all_to_all): exact mode bit-identical (every contribution computed and rounded as on one GPU,
 combined in the same slot order); partials mode within the bf16 tolerance (1e-2 relative); no
 device error bits (no arrival wait ran out)."""
 import pytest
@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["p2p", "collective"])
+@pytest.mark.parametrize("transport", ["push", "copy", "collective"])
 @pytest.mark.parametrize("mode", ["exact", "partials"])
 @pytest.mark.parametrize("moe_type", [0, 1])
 def test_expert_parallel_two_gpus(moe_type, mode, transport):
