@@ -258,7 +258,16 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     // GEMM-1
     CUtensorMap mA, mB0, mB1;
     const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
-    const int bn1 = (mode1 == kModeG1Single && I % 256 == 0) ? 256 : 128;
+    // Output tiles as wide as the shape allows, also for decode-sized calls: a tile's weight
+    // stream runs at (bytes in flight per SM) / latency, which grows with the tile width, so
+    // narrower tiles on more SMs move the weights no faster and add waves (measured on B200:
+    // 64-wide gate|up tiles took GEMM-1 of a top-2 decode step at 8 tokens to 92 us).
+    auto pick_bn = [](int n, int widest, int narrowest) {
+      int bn = widest;
+      while (bn > narrowest && n % bn != 0) bn /= 2;
+      return bn;
+    };
+    const int bn1 = mode1 == kModeG1Dual ? pick_bn(I, 128, 64) : pick_bn(I, 256, 128);
     const int cols1 = sm100_out_cols(mode1, bn1);
     // GEMM-1 gathers its A rows with cp.async; mA is an unused placeholder there
     bool ok = make_map_2d(&mA, dtype, input, H, T, 64, 64) &&
@@ -290,7 +299,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     if (ev) cudaEventRecord(ev[2], stream);
     // GEMM-2
     const int mode2 = moe_type == 0 ? kModeG2MN : kModeG2K;
-    const int bn2 = H % 256 == 0 ? 256 : 128;
+    const int bn2 = pick_bn(H, 256, 128);
     if (ok) {
       ok = make_map_2d(&mA, dtype, inter, I, static_cast<uint64_t>(rows), 64, 128);
       if (mode2 == kModeG2MN)

@@ -53,11 +53,12 @@ constexpr size_t kSm100SmemMax = 232448 - 1024;
 template <int MODE, int BN>
 struct TileCfg {
   static constexpr bool kGather = (MODE == kModeG1Dual || MODE == kModeG1Single);
-  // Qwen3's gate and up tiles sit back to back in shared memory (boxes 0-1 gate, 2-3 up, one
-  // 8 KB box stride), so one N=256 MMA computes both accumulators, reading the A tile once.
-  static constexpr int kMmaN = (MODE == kModeG1Dual) ? 256 : BN;
-  static constexpr int kOutCols = (MODE == kModeG1Dual) ? 128 : BN;
-  static constexpr int kBBytes = (MODE == kModeG1Dual) ? 2 * 128 * kBK * 2 : BN * kBK * 2;
+  // Qwen3's gate and up tiles of the same BN intermediate columns sit back to back in shared
+  // memory (BN/64 gate boxes, then BN/64 up boxes, one 8 KB box stride), so one N = 2*BN MMA
+  // computes both accumulators, reading the A tile once.
+  static constexpr int kMmaN = (MODE == kModeG1Dual) ? 2 * BN : BN;
+  static constexpr int kOutCols = BN;
+  static constexpr int kBBytes = (MODE == kModeG1Dual) ? 2 * BN * kBK * 2 : BN * kBK * 2;
   // bytes the TMA copies of one stage deliver (A too when it is not gathered)
   static constexpr uint32_t kTxBytes = kBBytes + (kGather ? 0 : kAStageBytes);
   // arrivals that complete a full barrier: the TMA thread + every gather thread
@@ -220,10 +221,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           if (!C::kGather) tma_load_2d(a_dst, &tmA, full, kc, ti.row_base);
           if (MODE == kModeG1Dual) {
             const int krow = ti.e * p.K + kc;
-            tma_load_2d(b_dst, &tmB0, full, ti.n0, krow);
-            tma_load_2d(b_dst + 8192, &tmB0, full, ti.n0 + 64, krow);
-            tma_load_2d(b_dst + 16384, &tmB1, full, ti.n0, krow);
-            tma_load_2d(b_dst + 24576, &tmB1, full, ti.n0 + 64, krow);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_2d(b_dst + j * 8192, &tmB0, full, ti.n0 + j * 64, krow);
+              tma_load_2d(b_dst + (BN / 64 + j) * 8192, &tmB1, full, ti.n0 + j * 64, krow);
+            }
           } else if (MODE == kModeG1Single || MODE == kModeG2MN) {
             const int krow = ti.e * p.K + kc;
 #pragma unroll
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
           if (MODE == kModeG1Dual) {
             uint32_t gv[32], uv[32];
             tmem_ld_32x32b_x32(tb + cc + 32 * h, gv);
-            tmem_ld_32x32b_x32(tb + 128 + cc + 32 * h, uv);
+            tmem_ld_32x32b_x32(tb + C::kOutCols + cc + 32 * h, uv);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i)
@@ -466,7 +468,7 @@ int sm100_max_experts() {
   return static_cast<int>((kSm100SmemMax - kSm100SmemBase) / (2 * sizeof(int32_t))) - 2;
 }
 
-int sm100_out_cols(int mode, int bn) { return mode == kModeG1Dual ? 128 : bn; }
+int sm100_out_cols(int mode, int bn) { return bn; }
 
 template <typename T, int MODE, int BN>
 static bool set_attr_one() {
@@ -478,6 +480,7 @@ static bool set_attr_one() {
 template <typename T>
 static bool set_attr_t() {
   bool ok = set_attr_one<T, kModeG1Dual, 128>();
+  ok &= set_attr_one<T, kModeG1Dual, 64>();
   ok &= set_attr_one<T, kModeG1Single, 128>();
   ok &= set_attr_one<T, kModeG1Single, 256>();
   ok &= set_attr_one<T, kModeG2MN, 128>();
@@ -503,6 +506,7 @@ static int launch_t(int mode, int bn, const CUtensorMap& a, const CUtensorMap& b
   return 0;
   switch (mode) {
     case kModeG1Dual:
+      if (bn == 64) { CMOE_SM100(kModeG1Dual, 64) }
       CMOE_SM100(kModeG1Dual, 128)
     case kModeG1Single:
       if (bn == 256) { CMOE_SM100(kModeG1Single, 256) }
