@@ -151,19 +151,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Row gather: four rows r0..r3 of a 2-D map whose box is one row high, columns from c0.  The
-// rows land back to back in shared memory.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int32_t c0, int32_t r0, int32_t r1, int32_t r2,
-                                            int32_t r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2),
-      "r"(r3)
-      : "memory");
-}
-
 // 16-byte global -> shared copy through L2 only (cp.async.cg); completion is tracked by
 // cp_async_mbar_arrive_noinc on an mbarrier whose expected count includes this thread.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {

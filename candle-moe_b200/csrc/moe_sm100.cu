@@ -105,20 +105,6 @@ __device__ __forceinline__ int next_tile_from_ring(uint64_t* tfull, uint64_t* te
   return t;
 }
 
-template <typename T>
-__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w;
-    w.x = pack2<T>(v[q * 8 + 0], v[q * 8 + 1]);
-    w.y = pack2<T>(v[q * 8 + 2], v[q * 8 + 3]);
-    w.z = pack2<T>(v[q * 8 + 4], v[q * 8 + 5]);
-    w.w = pack2<T>(v[q * 8 + 6], v[q * 8 + 7]);
-    d[q] = w;
-  }
-}
-
 template <typename T, int MODE, int BN>
 __global__ void __launch_bounds__(kSm100Threads, 1)
     sm100_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
