@@ -137,6 +137,164 @@ __global__ void __launch_bounds__(kSimtThreads) simt_grouped_gemm_kernel(SimtPar
   }
 }
 
+// f32 operands whose rows start on 16-byte boundaries (K and N multiples of 4, aligned bases):
+// float4 global loads, the next 16-deep K slice loaded into registers while the current one is
+// multiplied out of shared memory (two buffers, one barrier per slice), 64 x BN tiles with 4 x 8
+// (BN = 128) or 4 x 4 (BN = 64) outputs per thread; the column groups of a thread sit 64 apart.
+// Same modes, tile list, rounding and epilogue as simt_grouped_gemm_kernel.
+template <int MODE, int BN>
+__global__ void __launch_bounds__(kSimtThreads) simt_f32v_kernel(SimtParams p) {
+  constexpr int BM = 64, BK = 16, TN = BN / 16, NB = BN / 64;  // NB float4 of B per thread
+  __shared__ __align__(16) float As[2][BK][BM + 4];
+  __shared__ __align__(16) float Bs[2][BK][BN + 4];
+  __shared__ __align__(16) float Us[MODE == 0 ? 2 : 1][MODE == 0 ? BK : 1][BN + 4];
+  __shared__ int64_t s_arow[BM];
+
+  const int mt = blockIdx.y;
+  const int E = p.E, N = p.N, K = p.K;
+  if (mt >= __ldg(p.tile_prefix + E)) return;
+  const int e = expert_of_tile(p.tile_prefix, E, mt);
+  const int m0 = (mt - __ldg(p.tile_prefix + e)) * BM;
+  const int row_base = __ldg(p.offsets + e) + m0;
+  const int cnt = __ldg(p.offsets + e + 1) - __ldg(p.offsets + e);
+  const int valid = min(BM, cnt - m0);
+  const int n0 = blockIdx.x * BN;
+  const int tid = threadIdx.x;
+  if (tid < BM) {
+    const int r = min(tid, valid - 1);
+    s_arow[tid] = (MODE <= 1) ? static_cast<int64_t>(__ldg(p.sorted_token + row_base + r))
+                              : static_cast<int64_t>(row_base + r);
+  }
+  __syncthreads();
+
+  const float* A = static_cast<const float*>(p.a);
+  const size_t wstride = static_cast<size_t>(K) * N;
+  const float* B0 = static_cast<const float*>(p.b0) + static_cast<size_t>(e) * wstride;
+  const float* B1 = MODE == 0 ? static_cast<const float*>(p.b1) + static_cast<size_t>(e) * wstride
+                              : nullptr;
+  // loader coordinates: A row tid/4, k quad (tid%4)*4; B float4 index tid + 256*i
+  const int a_r = tid >> 2, a_c = (tid & 3) * 4;
+  const float* a_src = A + s_arow[a_r] * K + a_c;
+  float4 ra, rb[NB], ru[NB];
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto load_regs = [&](int k0) {
+    ra = k0 + a_c < K ? __ldg(reinterpret_cast<const float4*>(a_src + k0)) : z4;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int idx = tid + kSimtThreads * i;
+      if (MODE == 3) {  // B[k][n] = U[n][k]: 4 consecutive k of one n
+        const int n = n0 + (idx >> 2), kk = k0 + (idx & 3) * 4;
+        rb[i] = (n < N && kk < K)
+                    ? __ldg(reinterpret_cast<const float4*>(B0 + static_cast<size_t>(n) * K + kk))
+                    : z4;
+      } else {  // 4 consecutive n of one k
+        const int kk = k0 + idx / (BN / 4), n = n0 + (idx % (BN / 4)) * 4;
+        const bool ok = kk < K && n < N;
+        const size_t o = static_cast<size_t>(kk) * N + n;
+        rb[i] = ok ? __ldg(reinterpret_cast<const float4*>(B0 + o)) : z4;
+        if (MODE == 0) ru[i] = ok ? __ldg(reinterpret_cast<const float4*>(B1 + o)) : z4;
+      }
+    }
+  };
+  auto store_smem = [&](int buf) {
+    As[buf][a_c + 0][a_r] = ra.x;
+    As[buf][a_c + 1][a_r] = ra.y;
+    As[buf][a_c + 2][a_r] = ra.z;
+    As[buf][a_c + 3][a_r] = ra.w;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int idx = tid + kSimtThreads * i;
+      if (MODE == 3) {
+        const int n = idx >> 2, kq = (idx & 3) * 4;
+        Bs[buf][kq + 0][n] = rb[i].x;
+        Bs[buf][kq + 1][n] = rb[i].y;
+        Bs[buf][kq + 2][n] = rb[i].z;
+        Bs[buf][kq + 3][n] = rb[i].w;
+      } else {
+        const int kk = idx / (BN / 4), n = (idx % (BN / 4)) * 4;
+        *reinterpret_cast<float4*>(&Bs[buf][kk][n]) = rb[i];
+        if (MODE == 0) *reinterpret_cast<float4*>(&Us[buf][kk][n]) = ru[i];
+      }
+    }
+  };
+
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][TN], acc2[MODE == 0 ? 4 : 1][MODE == 0 ? TN : 1];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      acc[i][j] = 0.f;
+      if (MODE == 0) acc2[i][j] = 0.f;
+    }
+
+  load_regs(0);
+  store_smem(0);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = 0; k0 < K; k0 += BK) {
+    const bool more = k0 + BK < K;
+    if (more) load_regs(k0 + BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      float b[TN], u[MODE == 0 ? TN : 1];
+#pragma unroll
+      for (int g = 0; g < TN / 4; ++g) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][kk][g * 64 + tx * 4]);
+        b[g * 4 + 0] = b4.x;
+        b[g * 4 + 1] = b4.y;
+        b[g * 4 + 2] = b4.z;
+        b[g * 4 + 3] = b4.w;
+        if (MODE == 0) {
+          const float4 u4 = *reinterpret_cast<const float4*>(&Us[buf][kk][g * 64 + tx * 4]);
+          u[g * 4 + 0] = u4.x;
+          u[g * 4 + 1] = u4.y;
+          u[g * 4 + 2] = u4.z;
+          u[g * 4 + 3] = u4.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+          if (MODE == 0) acc2[i][j] = fmaf(a[i], u[j], acc2[i][j]);
+        }
+    }
+    if (more) store_smem(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+
+  float* out = static_cast<float*>(p.out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = ty * 4 + i;
+    if (r >= valid) continue;
+    int64_t orow;
+    float wgt = 1.f;
+    if (MODE <= 1) {
+      orow = row_base + r;
+    } else {
+      orow = __ldg(p.sorted_flat + row_base + r);
+      if (p.out_row) orow = __ldg(p.out_row + orow);
+      wgt = __ldg(p.sorted_w + row_base + r);
+    }
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int n = n0 + (j / 4) * 64 + tx * 4 + (j % 4);
+      if (n >= N) continue;
+      float v;
+      if (MODE == 0) v = act_apply(acc[i][j], p.act) * acc2[i][j];
+      else if (MODE == 1) v = act_apply(acc[i][j], p.act);
+      else v = acc[i][j] * wgt;
+      out[orow * N + n] = v;
+    }
+  }
+}
+
 // out[t, :] = sum over slots j < k whose expert id is < E of slot[t*k + j, :], in slot order,
 // accumulated in f32 and rounded once.  V elements (16 bytes) per thread when H allows it.  KC
 // slots are handled per pass with all their loads in flight together (the expert ids first, then
@@ -197,8 +355,26 @@ __global__ void __launch_bounds__(256) combine_slots_kernel(const T* __restrict_
 
 // ---- host launchers --------------------------------------------------------------------------
 
+template <int BN>
+static void simt_f32v_launch(int mode, const SimtParams& p, int64_t mtile_bound, cudaStream_t s) {
+  dim3 grid((p.N + BN - 1) / BN, static_cast<unsigned>(mtile_bound));
+  switch (mode) {
+    case 0: simt_f32v_kernel<0, BN><<<grid, kSimtThreads, 0, s>>>(p); break;
+    case 1: simt_f32v_kernel<1, BN><<<grid, kSimtThreads, 0, s>>>(p); break;
+    case 2: simt_f32v_kernel<2, BN><<<grid, kSimtThreads, 0, s>>>(p); break;
+    default: simt_f32v_kernel<3, BN><<<grid, kSimtThreads, 0, s>>>(p); break;
+  }
+}
+
 template <typename T>
 static void simt_launch_t(int mode, const SimtParams& p, int64_t mtile_bound, cudaStream_t s) {
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (sizeof(T) == 4 && p.K % 4 == 0 && p.N % 4 == 0 && a16(p.a) && a16(p.b0) &&
+      (mode != 0 || a16(p.b1))) {
+    if (p.N >= 1024) simt_f32v_launch<128>(mode, p, mtile_bound, s);
+    else simt_f32v_launch<64>(mode, p, mtile_bound, s);
+    return;
+  }
   dim3 grid((p.N + kSimtBN - 1) / kSimtBN, static_cast<unsigned>(mtile_bound));
   switch (mode) {
     case 0: simt_grouped_gemm_kernel<T, 0><<<grid, kSimtThreads, 0, s>>>(p); break;
