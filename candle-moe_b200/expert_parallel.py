@@ -256,6 +256,20 @@ class _Landing:
             if grow[r] and r != self.rank:
                 self.addr[r] = self.ops.peer_open(bytes(gathered[r].cpu().numpy()), self.device)
 
+    def abandon(self):
+        """Local, non-collective release after a failed exchange (peers may be gone): unmap the
+        peers' buffers and free this rank's own."""
+        for r in range(self.world):
+            if self.addr[r] and r != self.rank:
+                self.ops.peer_close(self.addr[r], self.device)
+            self.addr[r] = 0 if r != self.rank else self.addr[r]
+        if self.addr[self.rank]:
+            self.local = None
+            self.ops.peer_free(self.addr[self.rank], self.device)
+            self.addr[self.rank] = 0
+        self.caps = [(0, 0)] * self.world
+        self.key = None
+
     def release(self):
         for r in range(self.world):
             if self.addr[r] and r != self.rank:
@@ -357,6 +371,23 @@ class ExpertParallelMoE:
         if self._landing is not None:
             self._landing.release()
             self._landing = None
+
+    def abandon(self):
+        """After a failed forward (a peer stopped signalling): release this rank's landing
+        buffers without any collective step."""
+        if self._landing is not None:
+            self._landing.abandon()
+            self._landing = None
+
+    def check_errors(self, device=None):
+        """Raise if an arrival wait of this device ran out since the last check (a peer never
+        signalled: the rows it should have sent are missing).  Synchronises the device."""
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        bits = candle_moe.device_error_bits(dev.index or 0, clear=True)
+        if bits & candle_moe.ERR_PEER_WAIT:
+            raise TimeoutError(f"expert-parallel exchange: an arrival wait ran out "
+                               f"(device error bits {bits:#x})")
 
     # ---- forward -----------------------------------------------------------------------------
     def _plan(self, x, routing_weights, expert_indices, C, Tc):

@@ -319,3 +319,51 @@ def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="
         result_q.put((rank, same and stats["error_bits"] == 0, diff, stats))
     finally:
         dist.destroy_process_group()
+
+
+class DroppingOps(CpuOracleOps):
+    """CPU ops whose rank `drop_rank` goes silent after its first arrival signal (its later
+    signals are lost, as when a peer stops), for the failure-detection test.  One lost signal
+    followed by a later one is not a failure: a later epoch implies the earlier chunks landed."""
+    drop_rank = 1
+    rank = 0
+    signals = 0
+
+    @classmethod
+    def peer_signal(cls, flag_addrs, value, stream):
+        cls.signals += 1
+        if cls.rank == cls.drop_rank and cls.signals > 1:
+            return  # lost
+        CpuOracleOps.peer_signal(flag_addrs, value, stream)
+
+
+def cpu_rank_dropped_signal(rank, world, port, transport, result_q):
+    """Rank 1's arrival signals stop after its first; every rank must stop with a timeout of its
+    arrival wait (not hang), then release its buffers without a collective step."""
+    import time as _time
+    import expert_parallel
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    T, H, I, E, k = 24, 16, 32, 8, 3
+    case = moe_case(31, T=T * world, H=H, I=I, E=E, k=k, moe_type=0, dtype="f32", wstd=0.1)
+    e0, e1 = expert_parallel.expert_range(E, world, rank)
+    DroppingOps.rank = rank
+    layer = expert_parallel.ExpertParallelMoE(E, k, 0, ops=DroppingOps(), chunks=3,
+                                              transport=transport, wait_timeout_s=1.0)
+    lo, hi = rank * T, (rank + 1) * T
+    t0 = _time.monotonic()
+    outcome = "finished"
+    try:
+        layer.forward(torch.from_numpy(case["x"][lo:hi].copy()),
+                      torch.from_numpy(case["gate"][e0:e1].copy()),
+                      torch.from_numpy(case["up"][e0:e1].copy()),
+                      torch.from_numpy(case["down"][e0:e1].copy()),
+                      torch.from_numpy(case["w"][lo:hi].copy()),
+                      torch.from_numpy(case["idx"][lo:hi].copy()), 0)
+    except TimeoutError as exc:
+        outcome = f"timeout: {exc}"
+    finally:
+        layer.abandon()
+    result_q.put((rank, outcome, _time.monotonic() - t0))
+    dist.destroy_process_group()

@@ -85,3 +85,24 @@ def test_p2p_layout_places_blocks_like_all_to_all():
                 back[s][b:b + n] = res[a:a + n]
     for s in range(G):
         assert back[s] == send[s]
+
+
+@pytest.mark.parametrize("transport", ["copy", "push"])
+def test_lost_arrival_signal_ends_in_timeouts_not_a_hang(transport):
+    """Failure detection without a GPU fault: rank 1's arrival signals stop after its first
+    (lost messages).  Rank 0's wait for the next chunk runs out after its 1 s limit, and rank 1,
+    whose returns from rank 0 then never come, runs out too; both release their buffers locally."""
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = ep_worker.free_port()
+    procs = [ctx.Process(target=ep_worker.cpu_rank_dropped_signal,
+                         args=(r, 2, port, transport, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0, p.exitcode
+    results = sorted(q.get() for _ in range(2))
+    for rank, outcome, seconds in results:
+        assert outcome.startswith("timeout"), (rank, outcome)
+        assert seconds < 30, (rank, seconds)
