@@ -260,9 +260,9 @@ class _Landing:
         """Local, non-collective release after a failed exchange (peers may be gone): unmap the
         peers' buffers and free this rank's own."""
         for r in range(self.world):
-            if self.addr[r] and r != self.rank:
+            if r != self.rank and self.addr[r]:
                 self.ops.peer_close(self.addr[r], self.device)
-            self.addr[r] = 0 if r != self.rank else self.addr[r]
+                self.addr[r] = 0
         if self.addr[self.rank]:
             self.local = None
             self.ops.peer_free(self.addr[self.rank], self.device)
