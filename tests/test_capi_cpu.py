@@ -104,3 +104,42 @@ def test_python_api_validation_matches_reference_messages():
     assert candle_moe.Activation.Gelu.to_int() == 1 and candle_moe.Activation.Relu.to_int() == 2
     with pytest.raises(TypeError):
         candle_moe.fused_moe_internal_dtype(torch.int8)
+
+
+def test_exchange_entry_points_reject_bad_arguments_without_a_gpu():
+    """The expert-parallel exchange entry points validate before any CUDA call."""
+    lib = candle_moe.lib()
+    p = ctypes.c_void_p(16)
+    two = (ctypes.c_void_p * 2)(16, 32)
+    many = (ctypes.c_void_p * 40)(*([16] * 40))
+    h = (ctypes.c_uint8 * candle_moe.PEER_HANDLE_BYTES)()
+    ptr = ctypes.c_void_p()
+    # peer buffers: null outputs, zero size, null handles and pointers
+    assert lib.moe_peer_alloc(0, ctypes.byref(ptr), h) == 1
+    assert lib.moe_peer_alloc(64, None, h) == 1
+    assert lib.moe_peer_open(None, ctypes.byref(ptr)) == 1
+    assert lib.moe_peer_close(None) == 1
+    assert lib.moe_peer_free(None) == 1
+    assert lib.moe_copy_async(None, p, 16, None) == 1
+    assert lib.moe_copy_async(p, p, 0, None) == 0  # nothing to copy
+    # arrival flags: more than 64 flags, misaligned flags, non-positive timeout
+    assert lib.moe_peer_signal(many, 65, 1, None) == 1
+    assert lib.moe_peer_signal((ctypes.c_void_p * 1)(18), 1, 1, None) == 1
+    assert lib.moe_peer_signal(None, 0, 1, None) == 0
+    assert lib.moe_peer_wait(ctypes.c_void_p(18), 1, 1, 1000, None) == 1
+    assert lib.moe_peer_wait(p, 65, 1, 1000, None) == 1
+    assert lib.moe_peer_wait(p, 1, 1, 0, None) == 1
+    # fused push kernels: rank counts beyond 32, null destination tables, inconsistent row maps
+    assert lib.moe_ep_push_pairs(p, p, p, p, 0, p, p, 2, 8, 33, 64, 1, many, many, None, 0,
+                                 None) == 1
+    assert lib.moe_ep_push_pairs(p, p, p, p, 0, p, p, 2, 8, 2, 64, 1, None, two, None, 0,
+                                 None) == 1
+    assert lib.moe_ep_push_pairs(p, p, p, p, -1, p, p, 2, 8, 2, 64, 1, two, two, None, 0,
+                                 None) == 1
+    first = (ctypes.c_int64 * 3)(0, 5, 4)  # not ascending
+    assert lib.moe_segment_sum_push(p, p, 4, 64, 1, 2, two, first, 0, None) == 1
+    first = (ctypes.c_int64 * 3)(0, 2, 3)  # does not end at num_segments
+    assert lib.moe_segment_sum_push(p, p, 4, 64, 1, 2, two, first, 0, None) == 1
+    assert lib.moe_segment_sum_push(p, p, 0, 64, 1, 2, two, first, 0, None) == 0  # no rows
+    # dest groups: assignment counts without a chunk count
+    assert lib.moe_ep_dest_groups(p, 4, 2, 8, 2, 2, p, 0, p, None) == 1
