@@ -513,6 +513,9 @@ def main():
                          "or NCCL all_to_all_single (collective)")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
+    ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="expert GEMM family: 0 automatic, 1 SIMT, 2 tensor cores, 3 "
+                         "automatic with one-CTA tensor-core kernels only")
     ap.add_argument("--tokens", type=int, default=0,
                     help="override the token count (small profiling cases)")
     args = ap.parse_args()
@@ -527,6 +530,9 @@ def main():
         run_reference(args, world, rank)
         return
     world, rank, local = dist_setup(args.gpus)
+    if args.gemm_path:
+        import candle_moe
+        candle_moe.set_gemm_path(args.gemm_path)
     try:
         run_ours(args, world, rank, local)
     finally:

@@ -23,8 +23,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                  "-I", os.path.join(ROOT, "include"), "-I", CSRC]
 EXTRA = {"router.cu": ["--use_fast_math"]}
-SOURCES = ["router.cu", "route_prep.cu", "moe_simt.cu", "moe_sm100.cu", "ep_kernels.cu", "peer.cu",
-           "capi.cu"]
+SOURCES = ["router.cu", "route_prep.cu", "moe_simt.cu", "moe_sm100.cu", "moe_sm100_pair.cu",
+           "ep_kernels.cu", "peer.cu", "capi.cu"]
 
 
 def _newest_header() -> float:

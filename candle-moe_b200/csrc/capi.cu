@@ -94,7 +94,8 @@ int init_device(int dev, DeviceState** out) {
     cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
     if (cudaMalloc(&d.err_word, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
-    const bool attrs_ok = route_prep_set_attributes() && sm100_set_attributes();
+    const bool attrs_ok =
+        route_prep_set_attributes() && sm100_set_attributes() && sm100_pair_set_attributes();
     cudaGetLastError();  // attribute failures are reported here, not by a later call
     if (!attrs_ok) return MOE_ERR_CUDA;
     if (!g_encode) {
@@ -316,9 +317,21 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.n_tiles = H / sm100_out_cols(mode2, bn2);
       const int64_t tiles = mtile_bound * p.n_tiles;
       const int sms = ds->num_sms - g_sm_reserve.load();
-      const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-      if (launch_sm100_gemm(static_cast<int>(dtype), mode2, bn2, mA, mB0, mB0, p, grid, stream))
-        ok = false;
+      bool done = false;
+      if (g_gemm_path.load() != 3 && !scatter && mode2 == kModeG2MN && bn2 == 256) {
+        // CTA pairs (cta_group::2): tiles of 256 rows, static schedule; shapes it does not take
+        // fall through to the one-CTA kernel, which also serves the scatter calls of the
+        // expert-parallel layer
+        const int64_t pair_tiles = (rows / 256 + (E < rows ? E : rows)) * p.n_tiles;
+        const int pairs = static_cast<int>(pair_tiles < sms / 2 ? pair_tiles : sms / 2);
+        done = launch_sm100_gemm2_pair(static_cast<int>(dtype), mA, mB0, p, pairs, stream) == 0;
+      }
+      if (!done) {
+        const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+        if (launch_sm100_gemm(static_cast<int>(dtype), mode2, bn2, mA, mB0, mB0, p, grid,
+                              stream))
+          ok = false;
+      }
     }
     if (!ok) st = MOE_ERR_CUDA;
     t_last_path = 2;
@@ -666,7 +679,7 @@ CMOE_API uint32_t moe_device_error_bits(int32_t device, int32_t clear) {
 }
 
 CMOE_API int32_t moe_set_gemm_path(int32_t path) {
-  if (path < 0 || path > 2) return -1;
+  if (path < 0 || path > 3) return -1;
   return g_gemm_path.exchange(path);
 }
 

@@ -113,6 +113,12 @@ int launch_ep_push_pairs(int dtype, const void* x, const int32_t* pair_token,
 int launch_segment_sum_push(int dtype, const void* in, const int64_t* start, int64_t R, int H,
                             int G, const EpPeerReturn& tab, int blocks, cudaStream_t s);
 
+// GEMM-2 (Qwen3 down projection) on CTA pairs, cta_group::2 (moe_sm100_pair.cu)
+size_t sm100_pair_smem_bytes(int num_experts);
+bool sm100_pair_set_attributes();
+int launch_sm100_gemm2_pair(int dtype, const CUtensorMap& a, const CUtensorMap& b,
+                            const Sm100Params& p, int pairs, cudaStream_t s);
+
 // arrival flags of the expert-parallel exchange (peer.cu)
 constexpr int kMaxPeerFlags = 64;
 struct PeerFlagPtrs {

@@ -1,0 +1,51 @@
+"""GEMM-2 on CTA pairs (cta_group::2, the default for Qwen3 fused calls) against the oracle and
+against the one-CTA kernels (GEMM path 3) on the same inputs: Qwen3 shapes whose hidden size is a multiple of 256, expert
+row counts that are not multiples of 256 (half-empty pair tiles), a k = 1 call, and the config-5
+shape on a token sample."""
+import numpy as np
+import pytest
+import torch
+
+import candle_moe
+import oracle
+from moe_testlib import check_close, from_torch, moe_case, to_torch
+
+pytestmark = pytest.mark.gpu
+
+CASES = [  # dtype, T, H, I, E, k
+    ("bf16", 300, 256, 256, 8, 2),
+    ("f16", 1000, 512, 384, 8, 2),
+    ("bf16", 64, 256, 128, 4, 1),
+    ("bf16", 2048, 2048, 768, 128, 8),
+]
+
+
+def _run(case, dtype, E, k, path):
+    prev = candle_moe.set_gemm_path(path)
+    try:
+        out = candle_moe.FusedMoE(E, k).forward(
+            to_torch(case["x"], dtype), to_torch(case["gate"], dtype), to_torch(case["up"], dtype),
+            to_torch(case["down"], dtype), torch.from_numpy(case["w"]).cuda(),
+            torch.from_numpy(case["idx"]).cuda(), 0)
+        torch.cuda.synchronize()
+        return out
+    finally:
+        candle_moe.set_gemm_path(prev)
+
+
+@pytest.mark.parametrize("dtype,T,H,I,E,k", CASES)
+def test_pair_gemm2_matches_oracle_and_one_cta_path(dtype, T, H, I, E, k):
+    candle_moe.device_error_bits(0, clear=True)
+    case = moe_case(77, T=T, H=H, I=I, E=E, k=k, moe_type=0, dtype=dtype, renormalize=True,
+                    bias_std=0.5)
+    pair = _run(case, dtype, E, k, 0)
+    assert candle_moe.device_error_bits(0) == 0
+    one = _run(case, dtype, E, k, 3)
+    got = oracle.to_f32(from_torch(pair, dtype), dtype)
+    rows = np.arange(T) if T <= 400 else np.random.default_rng(5).choice(T, 400, replace=False)
+    ref = oracle.moe_forward(case["x"][rows], case["gate"], case["up"], case["down"],
+                             case["w"][rows], case["idx"][rows], activation=0, moe_type=0,
+                             dtype=dtype)
+    check_close(got[rows], ref, 1e-2, f"pair {dtype} T={T}")
+    diff = (pair.float() - one.float()).abs().max().item()
+    assert diff <= 1e-2 * max(one.float().abs().max().item(), 1e-6), diff
