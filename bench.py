@@ -513,9 +513,10 @@ def main():
                          "or NCCL all_to_all_single (collective)")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
-    ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3],
+    ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3, 4],
                     help="expert GEMM family: 0 automatic, 1 SIMT, 2 tensor cores, 3 "
-                         "automatic with one-CTA tensor-core kernels only")
+                         "automatic with one-CTA tensor-core kernels only, 4 automatic with "
+                         "GEMM-1 on CTA pairs too (experimental)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="override the token count (small profiling cases)")
     args = ap.parse_args()

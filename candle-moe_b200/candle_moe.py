@@ -549,7 +549,8 @@ def device_error_bits(device: int = 0, clear: bool = False) -> int:
 
 def set_gemm_path(path: int) -> int:
     """0 automatic, 1 SIMT only, 2 tensor cores only, 3 automatic with one-CTA tensor-core
-    kernels only (no CTA pairs); returns the previous setting."""
+    kernels only (no CTA pairs), 4 automatic with GEMM-1 on CTA pairs too (experimental);
+    returns the previous setting."""
     return int(lib().moe_set_gemm_path(path))
 
 

@@ -293,8 +293,17 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.n_tiles = I / cols1;
       const int64_t tiles = mtile_bound * p.n_tiles;
       const int sms = ds->num_sms - g_sm_reserve.load();
+      bool done = false;
+      if (g_gemm_path.load() == 4 && !scatter && mode1 == kModeG1Dual && bn1 == 128) {
+        // CTA pairs (cta_group::2) as for GEMM-2 below; opt-in only: correct, but measured 1.9x
+        // slower than the one-CTA GEMM-1 at config 5
+        const int64_t pair_tiles = (rows / 256 + (E < rows ? E : rows)) * p.n_tiles;
+        const int pairs = static_cast<int>(pair_tiles < sms / 2 ? pair_tiles : sms / 2);
+        done = launch_sm100_gemm1_pair(static_cast<int>(dtype), mB0, mB1, p, pairs, stream) == 0;
+      }
       const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-      if (launch_sm100_gemm(static_cast<int>(dtype), mode1, bn1, mA, mB0, mB1, p, grid, stream))
+      if (!done &&
+          launch_sm100_gemm(static_cast<int>(dtype), mode1, bn1, mA, mB0, mB1, p, grid, stream))
         ok = false;
     }
     if (ev) cudaEventRecord(ev[2], stream);
@@ -679,7 +688,7 @@ CMOE_API uint32_t moe_device_error_bits(int32_t device, int32_t clear) {
 }
 
 CMOE_API int32_t moe_set_gemm_path(int32_t path) {
-  if (path < 0 || path > 3) return -1;
+  if (path < 0 || path > 4) return -1;
   return g_gemm_path.exchange(path);
 }
 

@@ -118,6 +118,8 @@ size_t sm100_pair_smem_bytes(int num_experts);
 bool sm100_pair_set_attributes();
 int launch_sm100_gemm2_pair(int dtype, const CUtensorMap& a, const CUtensorMap& b,
                             const Sm100Params& p, int pairs, cudaStream_t s);
+int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& u,
+                            const Sm100Params& p, int pairs, cudaStream_t s);
 
 // arrival flags of the expert-parallel exchange (peer.cu)
 constexpr int kMaxPeerFlags = 64;

@@ -1,5 +1,8 @@
-// GEMM-2 of the Qwen3 expert FFN (y = h.D_e x routing weight, D_e [I,H] MN-major) on CTA pairs:
-// tcgen05.mma.cta_group::2 with M = 256, so each SM stages only half of the B tile.
+// The Qwen3 expert GEMMs on CTA pairs: tcgen05.mma.cta_group::2 with M = 256, so each SM stages
+// only half of the B tile.  GEMM-2 (y = h.D_e x routing weight, D_e [I,H] MN-major) is the
+// default path for fused calls; GEMM-1 (gate|up with the activation epilogue, gathered rows) is
+// opt-in (GEMM path 4): it is correct but measured 1.9x slower than the one-CTA GEMM-1 at config 5.
+// The description below is GEMM-2's; GEMM-1's kernel says what differs.
 //
 // A cluster of two CTAs owns a pair tile: 256 sorted rows of one expert (each CTA 128 of them)
 // by 256 output columns (each CTA stages 128 of the B columns).  Per CTA a stage is 16 KB of A +
@@ -375,6 +378,301 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (warp == 2) tmem_dealloc_pair(tmem_base, 512);
 }
 
+// GEMM-1 of the Qwen3 FFN on CTA pairs: h = act(x.G_e) * (x.U_e) for 256 gathered rows of one
+// expert and 128 intermediate columns.  Each CTA gathers its own 128 token rows with cp.async into
+// the swizzled A layout (warps 2-3) and stages one half of the N = 256 B tile: the even CTA the
+// gate columns, the odd CTA the up columns; both CTAs' TMEM then hold gate (columns 0-127) and
+// up (128-255) of their own rows.  The even CTA's full barrier counts its producer (expected B
+// bytes of both CTAs), its 64 gather threads and one relay arrival: the odd CTA's warp 1 waits
+// for its own gather threads on its local full barrier, orders their generic-proxy writes before
+// the tensor core's async-proxy reads (fence.proxy.async) and arrives remotely.
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    sm100_gemm1_pair_kernel(const __grid_constant__ CUtensorMap tmG,
+                            const __grid_constant__ CUtensorMap tmU, const Sm100Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[kPStages];
+  __shared__ __align__(8) uint64_t bar_empty[kPStages];
+  __shared__ __align__(8) uint64_t bar_accf[2];
+  __shared__ __align__(8) uint64_t bar_acce[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t smem_base = (raw + 1023u) & ~1023u;
+  const uint32_t stage_out_base = smem_base + static_cast<uint32_t>(kPStages * kPStageBytes);
+  int32_t* s_tp = reinterpret_cast<int32_t*>(smem_raw + (smem_base - raw) +
+                                             static_cast<size_t>(kPStages) * kPStageBytes +
+                                             kPStageOut);
+  int32_t* s_off = s_tp + (p.E + 1);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = p.E;
+  const int num_kb = p.K / kPBK;
+  constexpr int kGatherArrivals = 64;
+
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) s_off[i] = __ldg(p.offsets + i);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      s_tp[e] = acc;
+      acc += (s_off[e + 1] - s_off[e] + 2 * kPBM - 1) / (2 * kPBM);
+    }
+    s_tp[E] = acc;
+    for (int st = 0; st < kPStages; ++st) {
+      // even CTA: producer + its gather threads + the odd CTA's relay; odd CTA: its gather
+      mbar_init(smem_addr(&bar_full[st]), rank == 0 ? 1 + kGatherArrivals + 1 : kGatherArrivals);
+      mbar_init(smem_addr(&bar_empty[st]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&bar_accf[b]), 1);
+      mbar_init(smem_addr(&bar_acce[b]), 8);
+    }
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmG);
+    tma_prefetch_desc(&tmU);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_addr(&s_tmem), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem;
+  const int total_tiles = s_tp[E] * p.n_tiles;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (B half)
+    if (lane == 0) {
+      const CUtensorMap* tmB = rank == 0 ? &tmG : &tmU;
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
+        const int mt = tile / p.n_tiles;
+        const int nt = tile - mt * p.n_tiles;
+        const int e = expert_of_tile_smem(s_tp, E, mt);
+        const int n0 = nt * (kPBN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
+                                 kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_local = smem_addr(&bar_full[stage]);
+          const uint32_t full0 = mapa_shared(full_local, 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_local, 2u * kPBStage);
+          const uint32_t b_dst = smem_base + stage * kPStageBytes + kPAStage;
+          const int krow = e * p.K + kb * kPBK;
+          tma_load_2d_pair(b_dst, tmB, full0, n0, krow);
+          tma_load_2d_pair(b_dst + 8192, tmB, full0, n0 + 64, krow);
+          if (++stage == kPStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------------------------------------------------------- MMA issuer (even CTA)
+      constexpr uint32_t idesc = umma_idesc(PairFmt<T>::v, 1u, 2 * kPBM, kPBN);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int lt = 0;
+      for (int tile = pair; ok && tile < total_tiles; tile += pairs, ++lt) {
+        const int buf = lt & 1;
+        const uint32_t par = static_cast<uint32_t>((lt >> 1) & 1) ^ 1u;
+        if (!mbar_wait_cluster_bounded(smem_addr(&bar_acce[buf]), par, &s_abort, p.err,
+                                       kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 256);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster_bounded(smem_addr(&bar_full[stage]), phase, &s_abort, p.err,
+                                         kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();  // this CTA's gathered rows (cp.async, generic proxy)
+          tc_fence_after();
+          const uint32_t a_base = smem_base + stage * kPStageBytes;
+          const uint32_t b_base = a_base + kPAStage;
+#pragma unroll
+          for (int ks = 0; ks < kPBK / 16; ++ks) {
+            const uint64_t adesc = umma_sdesc(a_base + ks * 32, 16, 1024);
+            const uint64_t bdesc = umma_sdesc(b_base + ks * 2048, 8192, 1024);
+            umma_f16_pair(d, adesc, bdesc, idesc, (kb | ks) != 0 ? 1u : 0u);
+          }
+          const uint32_t empty_local = smem_addr(&bar_empty[stage]);
+          umma_commit_pair(empty_local);
+          umma_commit_pair(mapa_shared(empty_local, 1));
+          if (++stage == kPStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t accf_local = smem_addr(&bar_accf[buf]);
+        umma_commit_pair(accf_local);
+        umma_commit_pair(mapa_shared(accf_local, 1));
+      }
+    } else if (lane == 0 && rank == 1) {
+      // ---------------------------------------------------------------- relay (odd CTA)
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const uint32_t full_local = smem_addr(&bar_full[stage]);
+          if (!mbar_wait_bounded(full_local, phase, &s_abort, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();  // the gathered rows before the even CTA's MMA reads them
+          mbar_arrive_remote(mapa_shared(full_local, 0));
+          if (++stage == kPStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------ A-row gather
+    const int g = threadIdx.x - 64;
+    const int c = g & 7;
+    const int q = g >> 3;
+    const T* x = static_cast<const T*>(p.a_rows);
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
+      const int mt = tile / p.n_tiles;
+      const int e = expert_of_tile_smem(s_tp, E, mt);
+      const int pm0 = (mt - s_tp[e]) * 2 * kPBM;
+      const int row_base = s_off[e] + pm0 + static_cast<int>(rank) * kPBM;
+      const int valid = min(kPBM, s_off[e + 1] - s_off[e] - pm0 - static_cast<int>(rank) * kPBM);
+      const T* src[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        // rows past the expert's last one repeat a valid row (their outputs are not written)
+        const int sr = valid > 0 ? row_base + min(q + 8 * i, valid - 1) : s_off[e] + pm0;
+        const int tok = __ldg(p.sorted_token + sr);
+        src[i] = x + static_cast<size_t>(tok) * p.K + c * 8;
+      }
+      const uint32_t dst_off = static_cast<uint32_t>(q * 128 + ((c ^ q) << 4));
+      for (int kb = 0; kb < num_kb; ++kb) {
+        bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
+                                     kErrWaitEmpty);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint32_t a_dst = smem_base + stage * kPStageBytes + dst_off;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cp_async16(a_dst + i * 8 * 128, src[i] + kb * kPBK);
+        cp_async_mbar_arrive_noinc(smem_addr(&bar_full[stage]));
+        if (++stage == kPStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp - 4;
+    const int r = q * 32 + lane;
+    T* out = static_cast<T*>(p.out);
+    const uint32_t stg = stage_out_base + static_cast<uint32_t>(q * 4096);
+    const int unit = lane & 7;
+    int lt = 0;
+    for (int tile = pair; tile < total_tiles; tile += pairs, ++lt) {
+      const int mt = tile / p.n_tiles;
+      const int nt = tile - mt * p.n_tiles;
+      const int e = expert_of_tile_smem(s_tp, E, mt);
+      const int m0 = (mt - s_tp[e]) * 2 * kPBM + static_cast<int>(rank) * kPBM;
+      const int row_base = s_off[e] + m0;
+      const int valid = min(kPBM, s_off[e + 1] - s_off[e] - m0);
+      const int n0 = nt * (kPBN / 2);
+      const int buf = lt & 1;
+      bool got = mbar_wait_bounded(smem_addr(&bar_accf[buf]), static_cast<uint32_t>((lt >> 1) & 1),
+                                   &s_abort, p.err, kErrWaitAccFull);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                          static_cast<uint32_t>(buf * 256);
+#pragma unroll 1
+      for (int cc = 0; cc < kPBN / 2; cc += 64) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tb + cc + 32 * h, gv);
+          tmem_ld_32x32b_x32(tb + kPBN / 2 + cc + 32 * h, uv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              v[i] = act_apply(__uint_as_float(gv[u * 8 + i]), p.act) *
+                     __uint_as_float(uv[u * 8 + i]);
+            const uint32_t addr = stg + lane * 128 + ((((4 * h + u) ^ (lane & 7))) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                         "r"(pack2<T>(v[0], v[1])), "r"(pack2<T>(v[2], v[3])),
+                         "r"(pack2<T>(v[4], v[5])), "r"(pack2<T>(v[6], v[7]))
+                         : "memory");
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const int srow = rr * 4 + (lane >> 3);
+          uint4 val;
+          const uint32_t addr = stg + srow * 128 + (((unit ^ (srow & 7))) << 4);
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                       : "r"(addr)
+                       : "memory");
+          if (q * 32 + srow < valid)
+            *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row_base + q * 32 + srow) * p.N +
+                                      n0 + cc + unit * 8) = val;
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t acce_local = smem_addr(&bar_acce[buf]);
+        if (rank == 0) mbar_arrive(acce_local);
+        else mbar_arrive_remote(mapa_shared(acce_local, 0));
+      }
+      (void)r;
+    }
+  }
+
+  __syncthreads();
+  if (s_abort) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem_base, 512);
+}
+
 }  // namespace
 
 size_t sm100_pair_smem_bytes(int num_experts) {
@@ -382,13 +680,32 @@ size_t sm100_pair_smem_bytes(int num_experts) {
 }
 
 bool sm100_pair_set_attributes() {
-  bool ok = cudaFuncSetAttribute(sm100_gemm2_pair_kernel<__nv_bfloat16>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kPSmemMax)) == cudaSuccess;
-  ok &= cudaFuncSetAttribute(sm100_gemm2_pair_kernel<__half>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kPSmemMax)) == cudaSuccess;
+  const int smax = static_cast<int>(kPSmemMax);
+  const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+  bool ok = cudaFuncSetAttribute(sm100_gemm2_pair_kernel<__nv_bfloat16>, attr, smax) == cudaSuccess;
+  ok &= cudaFuncSetAttribute(sm100_gemm2_pair_kernel<__half>, attr, smax) == cudaSuccess;
+  ok &= cudaFuncSetAttribute(sm100_gemm1_pair_kernel<__nv_bfloat16>, attr, smax) == cudaSuccess;
+  ok &= cudaFuncSetAttribute(sm100_gemm1_pair_kernel<__half>, attr, smax) == cudaSuccess;
   return ok;
+}
+
+// GEMM-1, Qwen3 (gate|up with the activation epilogue), on CTA pairs.  g / u: maps over gate and
+// up [E*H, I] with a 64 x 64 box; p.a_rows = x; p.out = the intermediate [rows, I]; p.n_tiles =
+// I / 128; pairs <= num_sms / 2.  Returns non-zero if the request does not fit this kernel.
+int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& u,
+                            const Sm100Params& p, int pairs, cudaStream_t s) {
+  if (pairs <= 0) return 0;
+  if (p.N % (kPBN / 2) != 0 || p.K % kPBK != 0) return 1;
+  const size_t smem = sm100_pair_smem_bytes(p.E);
+  if (smem > kPSmemMax) return 2;
+  const dim3 grid(2 * pairs), block(kPThreads);
+  if (dtype == kBF16)
+    sm100_gemm1_pair_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(g, u, p);
+  else if (dtype == kF16)
+    sm100_gemm1_pair_kernel<__half><<<grid, block, smem, s>>>(g, u, p);
+  else
+    return 1;
+  return 0;
 }
 
 // GEMM-2, Qwen3 (down projection, MN-major B), on CTA pairs.  a: A map (box 64 x 128 rows of the

@@ -218,7 +218,8 @@ uint32_t moe_device_error_bits(int32_t device, int32_t clear);
  * shape allows; the Qwen3 GEMM-2 of fused_moe / moe_fused_v2 runs on CTA pairs, cta_group::2 with
  * M = 256, when the hidden size is a multiple of 256), 1 = always the SIMT kernels, 2 = tensor
  * cores only (unsupported shapes then return MOE_ERR_UNSUPPORTED), 3 = as 0 but one-CTA
- * tensor-core kernels only.  Process-wide; returns the previous value (-1 for an unknown path).
+ * tensor-core kernels only, 4 = as 0 with the Qwen3 GEMM-1 on CTA pairs too (experimental: correct,
+ * slower).  Process-wide; returns the previous value (-1 for an unknown path).
  */
 int32_t moe_set_gemm_path(int32_t path);
 

@@ -1,7 +1,7 @@
-"""GEMM-2 on CTA pairs (cta_group::2, the default for Qwen3 fused calls) against the oracle and
-against the one-CTA kernels (GEMM path 3) on the same inputs: Qwen3 shapes whose hidden size is a multiple of 256, expert
-row counts that are not multiples of 256 (half-empty pair tiles), a k = 1 call, and the config-5
-shape on a token sample."""
+"""GEMM-2 (default) and GEMM-1 (opt-in path 4) on CTA pairs (cta_group::2) against the oracle and
+against the one-CTA kernels (GEMM path 3) on the same inputs: Qwen3 shapes whose hidden
+size is a multiple of 256, expert row counts that are not multiples of 256 (half-empty pair
+tiles), a k = 1 call, and the config-5 shape on a token sample."""
 import numpy as np
 import pytest
 import torch
@@ -33,12 +33,14 @@ def _run(case, dtype, E, k, path):
         candle_moe.set_gemm_path(prev)
 
 
+@pytest.mark.parametrize("path", [0, 4])
 @pytest.mark.parametrize("dtype,T,H,I,E,k", CASES)
-def test_pair_gemm2_matches_oracle_and_one_cta_path(dtype, T, H, I, E, k):
+def test_pair_gemms_match_oracle_and_one_cta_path(dtype, T, H, I, E, k, path):
+    """path 0: GEMM-2 on CTA pairs; path 4: GEMM-1 on CTA pairs too."""
     candle_moe.device_error_bits(0, clear=True)
     case = moe_case(77, T=T, H=H, I=I, E=E, k=k, moe_type=0, dtype=dtype, renormalize=True,
                     bias_std=0.5)
-    pair = _run(case, dtype, E, k, 0)
+    pair = _run(case, dtype, E, k, path)
     assert candle_moe.device_error_bits(0) == 0
     one = _run(case, dtype, E, k, 3)
     got = oracle.to_f32(from_torch(pair, dtype), dtype)
@@ -46,6 +48,6 @@ def test_pair_gemm2_matches_oracle_and_one_cta_path(dtype, T, H, I, E, k):
     ref = oracle.moe_forward(case["x"][rows], case["gate"], case["up"], case["down"],
                              case["w"][rows], case["idx"][rows], activation=0, moe_type=0,
                              dtype=dtype)
-    check_close(got[rows], ref, 1e-2, f"pair {dtype} T={T}")
+    check_close(got[rows], ref, 1e-2, f"pair path {path} {dtype} T={T}")
     diff = (pair.float() - one.float()).abs().max().item()
     assert diff <= 1e-2 * max(one.float().abs().max().item(), 1e-6), diff
