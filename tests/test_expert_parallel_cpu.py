@@ -106,3 +106,56 @@ def test_lost_arrival_signal_ends_in_timeouts_not_a_hang(transport):
     for rank, outcome, seconds in results:
         assert outcome.startswith("timeout"), (rank, outcome)
         assert seconds < 30, (rank, seconds)
+
+
+def test_p2p_layout_and_landing_regions_properties():
+    """For random rank / chunk counts and uneven traffic: every block a sender writes lies inside
+    the receiver's landing rows, blocks of different senders never overlap, the returned rows
+    fill the origin's return region exactly once, and the landing regions are 256-byte aligned
+    and large enough for the capacities."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+    import expert_parallel
+
+    @settings(max_examples=60, deadline=None)
+    @given(st.integers(1, 8), st.integers(1, 5), st.integers(0, 2 ** 31 - 1))
+    def check(G, C, seed):
+        rng = np.random.default_rng(seed)
+        allc = rng.integers(0, 7, size=(G, C, G, 3))
+        allc[..., 2] = allc[..., 0] + rng.integers(0, 3, size=(G, C, G))  # assignments >= pairs
+        for exact in (False, True):
+            a = allc.copy()
+            a[..., 1] = a[..., 2] if exact else a[..., 0]
+            send_start, recv_start, back_start, y_start = expert_parallel.p2p_layout(a)
+            pairs, back = a[..., 0], a[..., 1]
+            for d in range(G):
+                cover = np.zeros(int(pairs[:, :, d].sum()), dtype=int)
+                for c in range(C):
+                    for s in range(G):
+                        r0, n = recv_start[d, c, s], pairs[s, c, d]
+                        cover[r0:r0 + n] += 1
+                        assert r0 + n <= cover.size
+                        assert send_start[s, c, d] + n <= pairs[s].sum()
+                assert (cover == 1).all()
+            for s in range(G):
+                cover = np.zeros(int(back[s].sum()), dtype=int)
+                for c in range(C):
+                    for d in range(G):
+                        b0, n = back_start[s, c, d], back[s, c, d]
+                        cover[b0:b0 + n] += 1
+                        # the rows d returns for s sit inside d's chunk-c results
+                        assert y_start[d, c, s] + n <= back[:, c, d].sum()
+                assert (cover == 1).all()
+
+        L = expert_parallel._Landing(None, None, G, 0, "cpu")
+        L.key = (int(rng.integers(1, 64)) * 16, 2 * int(rng.integers(1, 9)) * 4)
+        L.caps = [(int(rng.integers(0, 500)), int(rng.integers(0, 500))) for _ in range(G)]
+        for r in range(G):
+            rows, meta, back0, total = L.regions(r)
+            row_b, meta_b = L.key
+            assert rows >= 4 * 2 * G and all(v % 256 == 0 for v in (rows, meta, back0, total))
+            assert meta >= rows + L.caps[r][0] * row_b
+            assert back0 >= meta + L.caps[r][0] * meta_b
+            assert total >= back0 + L.caps[r][1] * row_b
+
+    check()
