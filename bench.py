@@ -72,12 +72,16 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def load_traffic(kernel_key):
-    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+def load_profile(kernel_key):
+    """ncu figures of a kernel from the committed summaries (profiles/traffic.json): per-launch
+    DRAM bytes (`dram_bytes`), tensor-pipe activity (`tensor_pipe_pct`), the kernel's name and
+    the summary file they come from; {} when none was captured."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
-        return json.load(open(p)).get(kernel_key)
-    return None
+        v = json.load(open(p)).get(kernel_key)
+        if isinstance(v, dict):
+            return v
+    return {}
 
 
 class ClockSampler:
@@ -369,36 +373,76 @@ def run_ours(args, world, rank, local):
     if not router_only and ncalls:
         rows = layer.last_stats["assignments_received"] if ep else T * k
         n_up = 2 if moe_type == 0 else 1
+        elt = 4 if dtype == "f32" else 2
         flops = {"gemm1": 2.0 * rows * H * I * n_up, "gemm2": 2.0 * rows * I * H}
+        # algorithmic HBM bytes of one pass: each expert's weights once, each token row once,
+        # the intermediate written and read once, the (token, slot) rows written once (k > 1)
+        n_exp = layer.num_local if ep else E
+        algo_bytes = {
+            "gemm1": elt * (n_up * n_exp * H * I + T * H + rows * I),
+            "gemm2": elt * (n_exp * I * H + rows * I + (rows * H if k > 1 else T * H)),
+        }
         per_call = {p: phases[p] / ncalls for p in phases}
         per_step = {p: phases[p] / args.steps for p in phases}
         dom = max(("gemm1", "gemm2"), key=lambda p: per_call[p])
         # flops[] are per step; with expert parallelism a step makes several fused calls
-        achieved = flops[dom] / (per_step[dom] / 1e3) / 1e12
+        tflops = {p: flops[p] / (per_step[p] / 1e3) / 1e12 for p in ("gemm1", "gemm2")}
+        step_tflops = (flops["gemm1"] + flops["gemm2"]) / (ms_step / 1e3) / 1e12
         if dtype == "f32":
             # the f32 path runs on the FP32 pipes (SIMT kernel); no measured FP32 peak exists
             # on this pool, so the nominal one: 148 SMs x 128 lanes x 2 FLOP x 1965 MHz
             peak = 148 * 128 * 2 * 1.965e9 / 1e12
+            peak_sus = None
             kernel, bound, kind = "simt_grouped_gemm", "fp32", "nominal FP32 FFMA"
         else:
-            peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+            # the GEMMs run a few ms at a time between lighter kernels, at the SM clock the
+            # `clocks` key shows (near the maximum), so the denominator is the burst figure;
+            # the fraction of the power-capped sustained figure is given beside it
+            peak = peaks.get("bf16_tflops")
+            peak_sus = peaks.get("bf16_tflops_sustained")
             kernel, bound = "sm100_grouped_gemm", "tensor"
-            kind = f"{peak_kind} bf16 dense, sustained (kernel timed inside a long step)"
+            kind = (f"{peak_kind} bf16 dense, burst (cuBLAS 8192^3, best of 10); "
+                    f"MEASURED_PEAKS.json")
+        per_kernel = {}
+        for ph in ("gemm1", "gemm2"):
+            prof = load_profile(f"{args.config}:{ph}") if not ep else {}
+            per_kernel[ph] = {
+                "kernel": prof.get("kernel"), "ms_per_step": per_step[ph],
+                "tflops": tflops[ph], "frac": tflops[ph] / peak,
+                "frac_of_sustained": tflops[ph] / peak_sus if peak_sus else None,
+                "algorithmic_bytes": algo_bytes[ph],
+                "traffic": prof.get("dram_bytes"),
+                "tensor_pipe_active_pct": prof.get("tensor_pipe_pct"),
+                "profile": prof.get("source"),
+            }
         line["roofline"] = {
-            "kernel": f"{kernel} ({dom})", "bound": bound,
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_kind": kind,
-            "traffic": load_traffic(f"{args.config}:{dom}"),
+            "kernel": per_kernel[dom]["kernel"] or f"{kernel} ({dom})", "phase": dom,
+            "bound": bound, "achieved": tflops[dom], "peak": peak, "unit": "TFLOP/s",
+            "frac": tflops[dom] / peak, "peak_kind": kind,
+            "frac_of_sustained": tflops[dom] / peak_sus if peak_sus else None,
+            "sm_mhz_median": clk.get("sm_mhz"),
+            "traffic": per_kernel[dom]["traffic"],
+            "algorithmic_bytes": algo_bytes[dom],
+            "tensor_pipe_active_pct": per_kernel[dom]["tensor_pipe_active_pct"],
             "flops_per_step": flops[dom], "launches_per_step": ncalls // args.steps,
+            "kernels": per_kernel,
+            "step": {"tflops": step_tflops, "frac": step_tflops / peak,
+                     "note": "both GEMMs' FLOPs over the whole step (router, route "
+                             "preparation and combine included)"},
         }
         line["phases_ms"] = per_step
-        line["tflops_total"] = (flops["gemm1"] + flops["gemm2"]) / (ms_step / 1e3) / 1e12
+        line["tflops_total"] = step_tflops
     line["e2e"] = {"value": T * world / (e2e_ms / 1e3) if not router_only else e2e_ms * 1e3,
                    "unit": line["unit"], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                    "ms_per_step": e2e_ms, "host_wall_ms_per_step": wall_ms,
                    "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's compute"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not router_only:
         line["cpu_baseline"] = cpu_baseline(cfg, inp, target_s=args.cpu_seconds)
+    if world == 1 and args.config == "c5" and not args.tokens and not args.no_extra:
+        # the metric's other two figures, on their own BASELINE configs: config 1's router
+        # microseconds and config 4's decode step (8 tokens)
+        line["router_c1"] = measure_router_c1()
+        line["decode_c4_t8"] = measure_decode_c4(8)
     if ep:
         # non-zero when an arrival wait of the exchange ran out (a rank never signalled)
         line["device_error_bits"] = int(max_over_ranks(world,
@@ -408,10 +452,96 @@ def run_ours(args, world, rank, local):
         emit(line)
 
 
+def _graph_time_us(fn, reps, per_graph):
+    """Device time per call of fn (which launches library kernels on the current stream): the
+    calls are captured per_graph at a time into a CUDA graph, the graph is replayed `reps`
+    times between CUDA events on the launching stream.  Returns (us per call, launches per
+    call)."""
+    import torch
+    import candle_moe
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    l0 = candle_moe.kernel_launches()
+    with torch.cuda.graph(graph):
+        for _ in range(per_graph):
+            fn()
+    launches = (candle_moe.kernel_launches() - l0) / per_graph
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+    del graph
+    return us, launches
+
+
+def measure_router_c1():
+    """BASELINE config 1 (topk-softmax, [512, 8] f32 logits ~ N(0,1), top-2) through the drop-in
+    apply_topk_softmax_inplace: device microseconds per call, CUDA-graph replay (the published
+    reference figure, README.md:17, is wall-clock per call on an A40)."""
+    import torch
+    import candle_moe
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    T, E, k = 512, 8, 2
+    logits = torch.randn(T, E, generator=g, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    src = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    us, launches = _graph_time_us(
+        lambda: candle_moe.apply_topk_softmax_inplace(logits, w, idx, src), 50, 20)
+    nbytes = T * (4 * E + 12 * k)
+    return {"us_per_call": us, "tokens": T, "experts": E, "top_k": k,
+            "bytes_per_call": nbytes, "gb_per_s": nbytes / (us * 1e-6) / 1e9,
+            "timing": "CUDA-graph replay, 20 calls per graph x 50 replays, CUDA events",
+            "gpu_launches_per_call": launches}
+
+
+def measure_decode_c4(tokens=8, dtype="bf16"):
+    """BASELINE config 4 at decode size: Qwen3 SwiGLU, H4096, I1536, 8 experts, top-2,
+    renormalised, `tokens` tokens.  One step = router + fused forward, timed as a CUDA-graph
+    replay (the per-step host work of a Python loop would otherwise dominate).  Bound by the
+    weight read: 3*H*I*elt bytes for every expert the step routes to."""
+    import torch
+    import candle_moe
+    cfg = CONFIGS["c4" if dtype == "bf16" else "c4-f16"]
+    cfg = cfg[:3] + (tokens,) + cfg[4:]
+    _, moe_type, act, T, H, I, E, k, renorm, _ = cfg
+    inp = make_inputs(cfg, seed=0)
+    moe = candle_moe.FusedMoE(E, k, candle_moe.Activation(act))
+
+    def step():
+        w, idx, _ = candle_moe.topk_softmax(inp["logits"], k, renormalize=renorm)
+        return moe.forward(inp["x"], inp["gate"], inp["up"], inp["down"], w, idx, moe_type)
+
+    _, idx, _ = candle_moe.topk_softmax(inp["logits"], k, renormalize=renorm)
+    n_exp = int(torch.unique(idx).numel())
+    us, launches = _graph_time_us(step, 40, 10)
+    nbytes = 3 * H * I * 2 * n_exp + 2 * T * H * 2 + T * E * 4
+    peaks, kind = load_peaks()
+    del inp
+    torch.cuda.empty_cache()
+    return {"us_per_step": us, "tokens": T, "dtype": dtype, "experts_routed": n_exp,
+            "bytes_per_step": nbytes, "gb_per_s": nbytes / (us * 1e-6) / 1e9,
+            "hbm_frac": nbytes / (us * 1e-6) / 1e9 / peaks["hbm_gbs"],
+            "peak_kind": f"{kind} HBM copy", "gemm_path": candle_moe.last_gemm_path(),
+            "timing": "CUDA-graph replay, 10 steps per graph x 40 replays, CUDA events",
+            "gpu_launches_per_step": launches}
+
+
 def cpu_baseline(cfg, inp, target_s=10.0):
     """The reference algorithm (CPU oracle port, all host threads) on a token sample."""
     import numpy as np
     import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
     dtype, moe_type, act, T, H, I, E, k, renorm, _ = cfg
 
     def raw(t):
@@ -448,6 +578,8 @@ def run_reference(args, world, rank):
         return
     import numpy as np
     import oracle
+    # all host threads, whatever OMP_NUM_THREADS the launcher exported (torchrun sets 1)
+    oracle.set_num_threads(os.cpu_count() or 1)
     cfg = CONFIGS[args.config]
     dtype, moe_type, act, T, H, I, E, k, renorm, bias_std = cfg
     # the same seeded distributions as our arm, generated on the host
@@ -505,6 +637,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-sample", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config-1 router and config-4 decode figures of the default run")
     ap.add_argument("--ep-mode", choices=["partials", "exact"], default="partials",
                     help="expert-parallel return: per-rank partial sums or per-slot rows")
     ap.add_argument("--ep-transport", choices=["push", "copy", "collective"], default="push",

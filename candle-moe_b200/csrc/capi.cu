@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <climits>
 #include <cstdint>
@@ -35,6 +36,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceState {
   std::atomic<bool> ready{false};
   int num_sms = 0;
+  int max_pairs = 0;  // 2-CTA clusters of the pair GEMMs resident at once
   int cc_major = 0, cc_minor = 0;
   cudaMemPool_t pool = nullptr;
   uint32_t* err_word = nullptr;
@@ -98,6 +100,7 @@ int init_device(int dev, DeviceState** out) {
         route_prep_set_attributes() && sm100_set_attributes() && sm100_pair_set_attributes();
     cudaGetLastError();  // attribute failures are reported here, not by a later call
     if (!attrs_ok) return MOE_ERR_CUDA;
+    d.max_pairs = sm100_pair_max_clusters();
     if (!g_encode) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -169,6 +172,20 @@ int finish(int status) {
     if (e != cudaSuccess) status = MOE_ERR_CUDA;
   }
   return status;
+}
+
+// SMs the persistent tensor-core GEMMs may use: all but the reserve, and at least one (the
+// reserve is a performance hint; a GEMM is never skipped because of it).
+int gemm_sms(const DeviceState* ds) {
+  const int sms = ds->num_sms - g_sm_reserve.load();
+  return sms < 1 ? 1 : sms;
+}
+
+// 2-CTA clusters for the pair GEMMs: one per two usable SMs, no more than can be resident at
+// once (0: the pair kernels cannot run; the one-CTA kernel takes the GEMM).
+int pair_grid(const DeviceState* ds, int sms) {
+  const int pairs = sms / 2;
+  return pairs < ds->max_pairs ? pairs : ds->max_pairs;
 }
 
 bool sm100_shape_ok(int dtype, const void* x, const void* g, const void* u, const void* d,
@@ -292,13 +309,13 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.K = H;
       p.n_tiles = I / cols1;
       const int64_t tiles = mtile_bound * p.n_tiles;
-      const int sms = ds->num_sms - g_sm_reserve.load();
+      const int sms = gemm_sms(ds);
       bool done = false;
       if (g_gemm_path.load() == 4 && !scatter && mode1 == kModeG1Dual && bn1 == 128) {
         // CTA pairs (cta_group::2) as for GEMM-2 below; opt-in only: correct, but measured 1.9x
         // slower than the one-CTA GEMM-1 at config 5
         const int64_t pair_tiles = (rows / 256 + (E < rows ? E : rows)) * p.n_tiles;
-        const int pairs = static_cast<int>(pair_tiles < sms / 2 ? pair_tiles : sms / 2);
+        const int pairs = static_cast<int>(std::min<int64_t>(pair_tiles, pair_grid(ds, sms)));
         done = launch_sm100_gemm1_pair(static_cast<int>(dtype), mB0, mB1, p, pairs, stream) == 0;
       }
       const int grid = static_cast<int>(tiles < sms ? tiles : sms);
@@ -325,14 +342,14 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.K = I;
       p.n_tiles = H / sm100_out_cols(mode2, bn2);
       const int64_t tiles = mtile_bound * p.n_tiles;
-      const int sms = ds->num_sms - g_sm_reserve.load();
+      const int sms = gemm_sms(ds);
       bool done = false;
       if (g_gemm_path.load() != 3 && !scatter && mode2 == kModeG2MN && bn2 == 256) {
         // CTA pairs (cta_group::2): tiles of 256 rows, static schedule; shapes it does not take
         // fall through to the one-CTA kernel, which also serves the scatter calls of the
         // expert-parallel layer
         const int64_t pair_tiles = (rows / 256 + (E < rows ? E : rows)) * p.n_tiles;
-        const int pairs = static_cast<int>(pair_tiles < sms / 2 ? pair_tiles : sms / 2);
+        const int pairs = static_cast<int>(std::min<int64_t>(pair_tiles, pair_grid(ds, sms)));
         done = launch_sm100_gemm2_pair(static_cast<int>(dtype), mA, mB0, p, pairs, stream) == 0;
       }
       if (!done) {
@@ -391,6 +408,10 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
 }
 
 }  // namespace
+
+// Kernel launches made by entry points defined in other translation units.
+void add_launches(int64_t n) { g_launches += n; }
+
 }  // namespace cmoe
 
 using namespace cmoe;
@@ -444,7 +465,9 @@ CMOE_API int moe_route_prep(const uint32_t* expert_indices, const float* routing
                             int32_t* expert_offsets, int32_t* sorted_token_ids,
                             float* sorted_weights, void* stream) {
   if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
-  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  // an empty request reads nothing: only the offsets (all zero) are written
+  if ((num_tokens > 0 && (!expert_indices || !routing_weights)) || !expert_offsets)
+    return MOE_ERR_INVALID_ARG;
   if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
     return MOE_ERR_UNSUPPORTED;
   DeviceState* ds = nullptr;
@@ -474,7 +497,9 @@ CMOE_API int moe_route_prep_ex(const uint32_t* expert_indices, const float* rout
                                int32_t* expert_offsets, int32_t* sorted_token_ids,
                                float* sorted_weights, int32_t* sorted_flat, void* stream) {
   if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
-  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  // an empty request reads nothing: only the offsets (all zero) are written
+  if ((num_tokens > 0 && (!expert_indices || !routing_weights)) || !expert_offsets)
+    return MOE_ERR_INVALID_ARG;
   if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
     return MOE_ERR_UNSUPPORTED;
   DeviceState* ds = nullptr;

@@ -8,6 +8,10 @@
 
 namespace cmoe {
 
+// ---- capi.cu ---------------------------------------------------------------------------------
+// Adds n to the count moe_kernel_launches() reports (for entry points outside capi.cu).
+void add_launches(int64_t n);
+
 // ---- router.cu -------------------------------------------------------------------------------
 int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int num_experts,
                   int num_tokens, int k, int renorm, int num_sms, cudaStream_t stream);
@@ -116,6 +120,7 @@ int launch_segment_sum_push(int dtype, const void* in, const int64_t* start, int
 // GEMM-2 (Qwen3 down projection) on CTA pairs, cta_group::2 (moe_sm100_pair.cu)
 size_t sm100_pair_smem_bytes(int num_experts);
 bool sm100_pair_set_attributes();
+int sm100_pair_max_clusters();
 int launch_sm100_gemm2_pair(int dtype, const CUtensorMap& a, const CUtensorMap& b,
                             const Sm100Params& p, int pairs, cudaStream_t s);
 int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& u,

@@ -511,7 +511,7 @@ static int launch_t(int mode, int bn, const CUtensorMap& a, const CUtensorMap& b
 
 int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s) {
-  if (grid <= 0) return 0;
+  if (grid <= 0) return 3;  // never report a GEMM that did not run as done
   if (dtype == kBF16) return launch_t<__nv_bfloat16>(mode, bn, a, b0, b1, p, grid, s);
   if (dtype == kF16) return launch_t<__half>(mode, bn, a, b0, b1, p, grid, s);
   return 1;

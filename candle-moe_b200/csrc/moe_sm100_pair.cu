@@ -689,12 +689,36 @@ bool sm100_pair_set_attributes() {
   return ok;
 }
 
+// Clusters of two CTAs of the pair kernels that can be resident at once on the current device
+// (both kernels use the same block size and shared-memory budget).  The static tile schedule
+// hands pair p the tiles p, p + pairs, ...: a cluster that could not be resident would run its
+// whole list after the others, so the launchers' callers cap `pairs` with this.  0 on error.
+int sm100_pair_max_clusters() {
+  cudaLaunchConfig_t cfg = {};
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = kPSmemMax;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, sm100_gemm2_pair_kernel<__nv_bfloat16>, &cfg) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
 // GEMM-1, Qwen3 (gate|up with the activation epilogue), on CTA pairs.  g / u: maps over gate and
 // up [E*H, I] with a 64 x 64 box; p.a_rows = x; p.out = the intermediate [rows, I]; p.n_tiles =
 // I / 128; pairs <= num_sms / 2.  Returns non-zero if the request does not fit this kernel.
 int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& u,
                             const Sm100Params& p, int pairs, cudaStream_t s) {
-  if (pairs <= 0) return 0;
+  if (pairs <= 0) return 3;  // no cluster fits: the caller takes the one-CTA kernel
   if (p.N % (kPBN / 2) != 0 || p.K % kPBK != 0) return 1;
   const size_t smem = sm100_pair_smem_bytes(p.E);
   if (smem > kPSmemMax) return 2;
@@ -713,7 +737,7 @@ int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& 
 // pairs <= num_sms / 2.  Returns non-zero if the request does not fit this kernel.
 int launch_sm100_gemm2_pair(int dtype, const CUtensorMap& a, const CUtensorMap& b,
                             const Sm100Params& p, int pairs, cudaStream_t s) {
-  if (pairs <= 0) return 0;
+  if (pairs <= 0) return 3;  // no cluster fits: the caller takes the one-CTA kernel
   if (p.N % kPBN != 0 || p.K % kPBK != 0) return 1;
   const size_t smem = sm100_pair_smem_bytes(p.E);
   if (smem > kPSmemMax) return 2;

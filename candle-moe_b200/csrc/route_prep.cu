@@ -319,7 +319,9 @@ extern "C" __attribute__((visibility("default"))) int moe_route_prep_noalloc(
     float* sorted_weights, void* stream) {
   using namespace cmoe;
   if (num_tokens < 0 || topk <= 0 || num_experts <= 0) return MOE_ERR_INVALID_ARG;
-  if (!expert_indices || !routing_weights || !expert_offsets) return MOE_ERR_INVALID_ARG;
+  // an empty request reads nothing: only the offsets (all zero) are written
+  if ((num_tokens > 0 && (!expert_indices || !routing_weights)) || !expert_offsets)
+    return MOE_ERR_INVALID_ARG;
   if (num_experts > route_prep_max_experts() || num_tokens * topk > INT32_MAX)
     return MOE_ERR_UNSUPPORTED;
   const size_t need = route_prep_scratch_bytes(num_tokens * topk, num_experts);
@@ -331,5 +333,7 @@ extern "C" __attribute__((visibility("default"))) int moe_route_prep_noalloc(
                         expert_offsets, nullptr, sorted_token_ids, sorted_weights, nullptr,
                         scratch, static_cast<cudaStream_t>(stream)) != 0)
     return MOE_ERR_UNSUPPORTED;
-  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+  add_launches(need ? 3 : 1);
+  return MOE_OK;
 }

@@ -48,6 +48,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_activation.restype = F
         L.oracle_num_threads.argtypes = []
         L.oracle_num_threads.restype = I
+        L.oracle_set_num_threads.argtypes = [I]
+        L.oracle_set_num_threads.restype = I
         L.oracle_convert_to_f32.argtypes = [P, I, SZ, P]
         L.oracle_convert_to_f32.restype = None
         L.oracle_convert_from_f32.argtypes = [P, I, SZ, P]
@@ -65,6 +67,11 @@ def _ptr(a: np.ndarray | None):
 
 def num_threads() -> int:
     return lib().oracle_num_threads()
+
+
+def set_num_threads(n: int) -> int:
+    """Use n OpenMP threads from now on (n <= 0: unchanged); returns the resulting count."""
+    return lib().oracle_set_num_threads(n)
 
 
 # ---------------------------------------------------------------------------------------------

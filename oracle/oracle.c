@@ -437,3 +437,16 @@ EXPORT int oracle_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Threads the OpenMP loops above use from now on (n <= 0 leaves the setting unchanged); returns
+ * the resulting count.  The CPU baselines set it to the host's core count explicitly, so that
+ * an inherited OMP_NUM_THREADS (torchrun exports 1) does not shrink them. */
+EXPORT int oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}

@@ -2,6 +2,9 @@
 generator), host<->torch conversion of raw bf16/f16 storage, and the tolerance rule."""
 from __future__ import annotations
 
+import json
+import os
+
 import numpy as np
 
 import oracle
@@ -54,13 +57,50 @@ def rel_tol(dtype: str) -> float:
     return 1e-4 if dtype == "f32" else 1e-2
 
 
+PARITY_LOG = os.environ.get("CMOE_PARITY_LOG")
+
+
+def error_report(got: np.ndarray, ref: np.ndarray) -> dict:
+    """Error figures of one comparison: max |got-ref| / rms(ref) (the scaled form), and the pure
+    element-wise relative error |got-ref| / |ref| -- its maximum over the non-cancelling elements
+    (|ref| >= rms(ref), where a relative error is meaningful), and the fraction of ALL elements
+    whose pure relative error is within 1e-2 and within 1e-4."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    diff = np.abs(got - ref)
+    scale = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    big = np.abs(ref) >= max(scale, 1e-30)
+    rel = diff / np.maximum(np.abs(ref), 1e-30)
+    return {
+        "max_err_of_rms": float(diff.max() / max(scale, 1e-30)) if diff.size else 0.0,
+        "max_rel_noncancelling": float(rel[big].max()) if big.any() else 0.0,
+        "noncancelling": int(big.sum()),
+        "frac_rel_le_1e-2": float(np.mean(rel <= 1e-2)) if rel.size else 1.0,
+        "frac_rel_le_1e-4": float(np.mean(rel <= 1e-4)) if rel.size else 1.0,
+        "elements": int(ref.size),
+    }
+
+
 def check_close(got: np.ndarray, ref: np.ndarray, rtol: float, what: str = ""):
     """Element-wise |got-ref| <= rtol*|ref| + rtol*rms(ref) (relative error at the data's
-    scale; the rms term keeps cancellation-sized outputs from failing a pure relative test)."""
+    scale; the rms term keeps cancellation-sized outputs from failing a pure relative test).
+
+    The pure element-wise relative error |got-ref| / |ref| is reported beside it (error_report)
+    and bounded by 2*rtol on every non-cancelling element (|ref| >= rms(ref)): for f16/bf16 one
+    unit in the last place is 0.4-0.8 % of a value, and a contribution that the reference rounds
+    to the operand type before the slots are summed can be larger than the sum itself, so a
+    single rounding flip of one contribution can exceed 1e-2 of the sum on its own.
+
+    Returns max |got-ref| / rms(ref); with CMOE_PARITY_LOG set, appends one JSON line per
+    comparison (the error_report figures) to that file."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     assert got.shape == ref.shape, (got.shape, ref.shape)
     assert np.all(np.isfinite(got)), f"{what}: non-finite output"
+    rep = error_report(got, ref)
+    if PARITY_LOG:
+        with open(PARITY_LOG, "a") as f:
+            f.write(json.dumps({"case": what, "rtol": rtol, **rep}) + "\n")
     scale = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
     atol = rtol * max(scale, 1e-30)
     diff = np.abs(got - ref)
@@ -71,4 +111,7 @@ def check_close(got: np.ndarray, ref: np.ndarray, rtol: float, what: str = ""):
             f"{what}: {int(bad.sum())}/{bad.size} elements out of tolerance (rtol={rtol}); "
             f"worst at flat {i}: got={got.flat[i]:.6g} ref={ref.flat[i]:.6g} "
             f"max_abs={diff.max():.3g} scale={scale:.3g}")
-    return float(diff.max() / max(scale, 1e-30)) if diff.size else 0.0
+    assert rep["max_rel_noncancelling"] <= 2 * rtol, (
+        f"{what}: pure relative error {rep['max_rel_noncancelling']:.3g} > {2 * rtol} on a "
+        f"non-cancelling element ({rep})")
+    return rep["max_err_of_rms"]

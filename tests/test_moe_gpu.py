@@ -134,9 +134,15 @@ def test_zero_tokens():
 # BASELINE-shaped configs at full size, checked on a seeded sample of tokens (each output row
 # depends only on its own token, so the oracle runs on the sampled rows alone).
 FULL = [
+    ("c3-nomic-bf16-T64", "bf16", 1, 1, 64, 768, 3072, 8, 2, 0.0),
     ("c3-nomic-bf16-T4096", "bf16", 1, 1, 4096, 768, 3072, 8, 2, 0.0),
-    ("c4-qwen3-f16-T64", "f16", 0, 0, 64, 4096, 1536, 8, 2, 0.0),
+    ("c3-nomic-bf16-T32768", "bf16", 1, 1, 32768, 768, 3072, 8, 2, 0.0),
     ("c4-qwen3-bf16-T8", "bf16", 0, 0, 8, 4096, 1536, 8, 2, 0.0),
+    ("c4-qwen3-f16-T8", "f16", 0, 0, 8, 4096, 1536, 8, 2, 0.0),
+    ("c4-qwen3-bf16-T64", "bf16", 0, 0, 64, 4096, 1536, 8, 2, 0.0),
+    ("c4-qwen3-f16-T64", "f16", 0, 0, 64, 4096, 1536, 8, 2, 0.0),
+    ("c4-qwen3-bf16-T32768", "bf16", 0, 0, 32768, 4096, 1536, 8, 2, 0.0),
+    ("c4-qwen3-f16-T32768", "f16", 0, 0, 32768, 4096, 1536, 8, 2, 0.0),
     ("c5-qwen3-bf16-T65536", "bf16", 0, 0, 65536, 2048, 768, 128, 8, 0.5),
 ]
 
@@ -149,3 +155,12 @@ def test_baseline_shapes_sampled(name, dtype, moe_type, act, T, H, I, E, k, bias
     assert used == 2
     rows = np.sort(np.random.default_rng(0).choice(T, size=min(T, 48), replace=False))
     check_close(got[rows], run_oracle(case, act, moe_type, dtype, rows), rel_tol(dtype), name)
+
+
+def test_c2_nomic_f32_full_shape_all_tokens():
+    """BASELINE config 2 at its own shape (f32 Nomic, 512 tokens, H768, I3072, 8 experts top-2,
+    GELU), every output element against the oracle at the f32 tolerance 1e-4."""
+    case = moe_case(2, T=512, H=768, I=3072, E=8, k=2, moe_type=1, dtype="f32")
+    got, used = run_gpu(case, 8, 2, 1, 1, "f32")
+    assert used == 1
+    check_close(got, run_oracle(case, 1, 1, "f32"), 1e-4, "c2-nomic-f32-T512")

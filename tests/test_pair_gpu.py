@@ -51,3 +51,19 @@ def test_pair_gemms_match_oracle_and_one_cta_path(dtype, T, H, I, E, k, path):
     check_close(got[rows], ref, 1e-2, f"pair path {path} {dtype} T={T}")
     diff = (pair.float() - one.float()).abs().max().item()
     assert diff <= 1e-2 * max(one.float().abs().max().item(), 1e-6), diff
+
+
+@pytest.mark.parametrize("reserve", [24, 127, 128])
+def test_large_sm_reserve_still_runs_every_gemm(reserve):
+    """moe_set_sm_reserve leaves SMs to concurrent kernels; however few it leaves (the pair
+    kernel needs two per cluster), both GEMMs still run and the output is unchanged."""
+    dtype, T, H, I, E, k = "bf16", 600, 512, 256, 8, 2
+    case = moe_case(91, T=T, H=H, I=I, E=E, k=k, moe_type=0, dtype=dtype, renormalize=True)
+    ref = _run(case, dtype, E, k, 0)
+    prev = candle_moe.set_sm_reserve(reserve)
+    try:
+        got = _run(case, dtype, E, k, 0)
+    finally:
+        candle_moe.set_sm_reserve(prev)
+    assert candle_moe.device_error_bits(0) == 0
+    assert torch.equal(got, ref)
