@@ -96,8 +96,8 @@ int init_device(int dev, DeviceState** out) {
     cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep);
     if (cudaMalloc(&d.err_word, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
-    const bool attrs_ok =
-        route_prep_set_attributes() && sm100_set_attributes() && sm100_pair_set_attributes();
+    const bool attrs_ok = route_prep_set_attributes() && sm100_set_attributes() &&
+                          sm100_pair_set_attributes() && decode_set_attributes();
     cudaGetLastError();  // attribute failures are reported here, not by a later call
     if (!attrs_ok) return MOE_ERR_CUDA;
     d.max_pairs = sm100_pair_max_clusters();
@@ -142,13 +142,30 @@ bool make_map_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, 
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Largest token count the decode kernels take by default (the reference's direct path takes
+// T <= 32 as well, moe.cu:481); above it the grouped GEMMs' 128-row tiles fill up.
+constexpr int64_t kDecodeMaxTokens = 32;
+
+// Rows per expert chunk of the decode kernels (moe_decode.cu) for this call, or 0 when the
+// grouped GEMMs serve it: f16/bf16 with 128-aligned H and I, at most kDecodeMaxTokens tokens
+// (any count with GEMM path 6), not with GEMM paths 1, 4 and 5.  Pointer alignment and the
+// device are checked by the caller (sm100_shape_ok).
+int decode_rows(int64_t T, int H, int I, int E, int dtype, int gpath) {
+  if (dtype == kF32 || H % 128 != 0 || I % 128 != 0 || E > decode_max_experts()) return 0;
+  if (gpath == 1 || gpath == 4 || gpath == 5) return 0;
+  if (T > kDecodeMaxTokens && gpath != 6) return 0;
+  return decode_chunk_rows(T);
+}
+
 // Workspace of one fused call (byte offsets into one buffer).
 struct FusedLayout {
   size_t offsets, tile_prefix, counters, sorted_token, sorted_flat, sorted_w, prep_scratch, inter,
-      slot, total;
+      slot, dec_part, dec_cnt, total;
+  int64_t dec_units1, dec_units2;  // unit-counter capacity of the decode GEMMs
 };
 
-FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype) {
+// dec_n: rows per chunk of the decode kernels (0: the grouped GEMMs run).
+FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype, int dec_n = 0) {
   const int64_t rows = T * k;
   const size_t elt = dtype == kF32 ? 4 : 2;
   FusedLayout L;
@@ -161,7 +178,19 @@ FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype) {
   L.sorted_w = o;       o += align256(sizeof(float) * rows);
   L.prep_scratch = o;   o += align256(route_prep_scratch_bytes(rows, E));
   L.inter = o;          o += align256(elt * static_cast<size_t>(rows) * I);
-  L.slot = o;           o += (k > 1) ? align256(elt * static_cast<size_t>(rows) * H) : 0;
+  // the decode kernels always combine through the (token, slot) rows, also for k = 1
+  L.slot = o;           o += (k > 1 || dec_n) ? align256(elt * static_cast<size_t>(rows) * H) : 0;
+  L.dec_part = o;
+  L.dec_units1 = L.dec_units2 = 0;
+  if (dec_n) {
+    // one region per GEMM: GEMM-2 starts while GEMM-1's last units are being finished
+    o += 2 * align256(decode_partial_bytes(dec_n, decode_max_grid()));
+    const int64_t chunks = rows / dec_n + (E < rows ? E : rows);
+    L.dec_units1 = chunks * (I / 128);
+    L.dec_units2 = chunks * (H / 128);
+  }
+  L.dec_cnt = o;
+  if (dec_n) o += align256(sizeof(uint32_t) * 4 * (L.dec_units1 + L.dec_units2 + H / 128));
   L.total = o;
   return L;
 }
@@ -224,11 +253,15 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
                    ds->cc_major == 10 && g_encode != nullptr;
   if (gpath == 1) use_sm100 = false;
   if (gpath == 2 && !use_sm100) return MOE_ERR_UNSUPPORTED;
-  const int bm = use_sm100 ? sm100_tile_m() : simt_tile_m();
 
   const bool scatter = out_row != nullptr;
+  // decode-sized calls: weight-streaming tensor-core kernels with the combine fused
+  const int dec_n = (use_sm100 && !scatter)
+                        ? decode_rows(T, H, I, E, static_cast<int>(dtype), gpath)
+                        : 0;
+  const int bm = dec_n ? dec_n : use_sm100 ? sm100_tile_m() : simt_tile_m();
   // scatter writes each contribution to its own output row: no slot buffer, no combine
-  FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype));
+  FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype), dec_n);
   if (scatter) L.total = L.slot;
   char* ws = static_cast<char*>(workspace);
   bool owned = false;
@@ -260,19 +293,82 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   if (ev) cudaEventRecord(ev[0], stream);
   int64_t launches = route_prep_scratch_bytes(rows, E) ? 3 : 1;
 
-  st = launch_route_prep(idx, rw, T, k, E, bm, offsets, tile_prefix, s_token, s_w, s_flat,
-                         prep_scratch, stream) == 0
-           ? MOE_OK
-           : MOE_ERR_UNSUPPORTED;
-  if (st == MOE_OK && k == 1 && !scatter)
+  if (dec_n) {
+    // the decode kernels' counters, zeroed before the route preparation so that GEMM-1 follows
+    // it directly (it is launched as the route preparation's programmatic dependent)
+    const size_t ncnt = 4 * static_cast<size_t>(L.dec_units1 + L.dec_units2 + H / 128);
+    if (cudaMemsetAsync(ws + L.dec_cnt, 0, ncnt * sizeof(uint32_t), stream) != cudaSuccess)
+      st = MOE_ERR_CUDA;
+  }
+  if (st == MOE_OK)
+    st = launch_route_prep(idx, rw, T, k, E, bm, offsets, tile_prefix, s_token, s_w, s_flat,
+                           prep_scratch, stream) == 0
+             ? MOE_OK
+             : MOE_ERR_UNSUPPORTED;
+  if (st == MOE_OK && k == 1 && !scatter && !dec_n)
     if (cudaMemsetAsync(output, 0, elt * static_cast<size_t>(T) * H, stream) != cudaSuccess)
       st = MOE_ERR_CUDA;
   if (ev) cudaEventRecord(ev[1], stream);
 
   uint32_t* counters = reinterpret_cast<uint32_t*>(ws + L.counters);
-  if (st == MOE_OK && use_sm100)
+  if (st == MOE_OK && dec_n) {
+    // ---------------------------------------------------------------- decode kernels (D1)
+    uint32_t* dcnt = reinterpret_cast<uint32_t*>(ws + L.dec_cnt);
+    const int grid = std::min(gemm_sms(ds), decode_max_grid());
+    DecodeParams p;
+    p.offsets = offsets;
+    p.chunk_prefix = tile_prefix;
+    p.sorted_token = s_token;
+    p.sorted_flat = s_flat;
+    p.sorted_w = s_w;
+    p.idx = idx;
+    p.partials = reinterpret_cast<float*>(ws + L.dec_part);
+    p.err = ds->err_word;
+    p.E = E;
+    p.act = act;
+    p.k = k;
+    p.num_tokens = static_cast<int>(T);
+    CUtensorMap mA0, mA1;
+    const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
+    bool ok = st == MOE_OK &&
+              make_map_2d(&mA0, dtype, gate, I, static_cast<uint64_t>(E) * H, 64, 64) &&
+              make_map_2d(&mA1, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 64);
+    if (ok) {
+      p.b_src = input;
+      p.out = inter;
+      p.final_out = nullptr;
+      p.unit_counter = dcnt;
+      p.tile_counter = nullptr;
+      p.M = I;
+      p.K = H;
+      ok = launch_decode_ffn(static_cast<int>(dtype), mode1, dec_n, mA0, mA1, p, grid, stream) == 0;
+    }
+    if (ev) cudaEventRecord(ev[2], stream);
+    const int mode2 = moe_type == 0 ? kModeG2MN : kModeG2K;
+    if (ok) {
+      ok = mode2 == kModeG2MN
+               ? make_map_2d(&mA0, dtype, down, H, static_cast<uint64_t>(E) * I, 64, 64)
+               : make_map_2d(&mA0, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 128);
+    }
+    if (ok) {
+      p.b_src = inter;
+      p.out = ws + L.slot;
+      p.final_out = output;
+      p.partials = reinterpret_cast<float*>(
+          ws + L.dec_part + align256(decode_partial_bytes(dec_n, decode_max_grid())));
+      p.unit_counter = dcnt + 4 * L.dec_units1;
+      p.tile_counter = dcnt + 4 * (L.dec_units1 + L.dec_units2);
+      p.M = H;
+      p.K = I;
+      ok = launch_decode_ffn(static_cast<int>(dtype), mode2, dec_n, mA0, mA0, p, grid, stream) == 0;
+    }
+    if (!ok && st == MOE_OK) st = MOE_ERR_CUDA;
+    if (ev) cudaEventRecord(ev[3], stream);
+    t_last_path = 3;
+  } else if (st == MOE_OK && use_sm100) {
     if (cudaMemsetAsync(counters, 0, 2 * sizeof(uint32_t), stream) != cudaSuccess) st = MOE_ERR_CUDA;
-  if (st == MOE_OK && use_sm100) {
+  }
+  if (st == MOE_OK && use_sm100 && !dec_n) {
     // GEMM-1
     CUtensorMap mA, mB0, mB1;
     const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
@@ -361,7 +457,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     }
     if (!ok) st = MOE_ERR_CUDA;
     t_last_path = 2;
-  } else if (st == MOE_OK) {
+  } else if (st == MOE_OK && !dec_n) {
     SimtParams p;
     p.out_row = nullptr;
     p.offsets = offsets;
@@ -395,9 +491,9 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     }
     t_last_path = 1;
   }
-  if (ev) cudaEventRecord(ev[3], stream);
+  if (ev && !dec_n) cudaEventRecord(ev[3], stream);
   launches += 2;
-  if (st == MOE_OK && k > 1 && !scatter) {
+  if (st == MOE_OK && k > 1 && !scatter && !dec_n) {
     launch_combine(static_cast<int>(dtype), slot, idx, T, k, H, E, output, ds->num_sms, stream);
     ++launches;
   }
@@ -653,8 +749,12 @@ CMOE_API size_t moe_fused_workspace_size(int64_t num_tokens, int32_t hidden_dim,
   if (num_tokens <= 0 || hidden_dim <= 0 || intermediate_dim <= 0 || num_experts <= 0 ||
       topk <= 0 || dtype > 2)
     return 0;
+  // the decode layout when the shape allows it (pointer alignment is only known at the call;
+  // a call that takes the grouped GEMMs needs less)
+  const int dec_n = decode_rows(num_tokens, hidden_dim, intermediate_dim, num_experts,
+                                static_cast<int>(dtype), g_gemm_path.load());
   return fused_layout(num_tokens, hidden_dim, intermediate_dim, num_experts, topk,
-                      static_cast<int>(dtype))
+                      static_cast<int>(dtype), dec_n)
       .total;
 }
 
@@ -713,7 +813,7 @@ CMOE_API uint32_t moe_device_error_bits(int32_t device, int32_t clear) {
 }
 
 CMOE_API int32_t moe_set_gemm_path(int32_t path) {
-  if (path < 0 || path > 4) return -1;
+  if (path < 0 || path > 6) return -1;
   return g_gemm_path.exchange(path);
 }
 

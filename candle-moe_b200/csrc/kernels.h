@@ -85,6 +85,34 @@ int sm100_out_cols(int mode, int bn);
 int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
 
+// ---- moe_decode.cu (D1: decode-sized calls, weights as the MMA's A operand, stream-K) -------
+struct DecodeParams {
+  const void* b_src;            // GEMM-1: x [T, K]; GEMM-2: intermediate [rows, K]
+  const int32_t* offsets;       // [E+2] route preparation offsets
+  const int32_t* chunk_prefix;  // [E+1] route preparation tile prefix, tile height = chunk rows
+  const int32_t* sorted_token;  // [rows]
+  const int32_t* sorted_flat;   // [rows]
+  const float* sorted_w;        // [rows]
+  const uint32_t* idx;          // [T*k] expert ids (GEMM-2's fused combine)
+  void* out;                    // GEMM-1: intermediate [rows, M]; GEMM-2: slot rows [T*k, M]
+  void* final_out;              // GEMM-2: output [T, M]
+  float* partials;              // decode_partial_bytes(): stream-K partial sums
+  uint32_t* unit_counter;       // [4 * units], zeroed before the launch
+  uint32_t* tile_counter;       // [4 * M/128], zeroed before the launch (GEMM-2)
+  uint32_t* err;                // device error word
+  int M;                        // weight output columns (I for GEMM-1, H for GEMM-2)
+  int K;                        // reduction length (H for GEMM-1, I for GEMM-2)
+  int E, act, k, num_tokens;
+};
+int decode_max_experts();
+int decode_max_grid();
+// Rows of one expert per MMA (the B operand's N) for a call of num_tokens tokens.
+int decode_chunk_rows(int64_t num_tokens);
+size_t decode_partial_bytes(int n, int grid);
+bool decode_set_attributes();
+int launch_decode_ffn(int dtype, int mode, int n, const CUtensorMap& a0, const CUtensorMap& a1,
+                      const DecodeParams& p, int grid, cudaStream_t s);
+
 // ---- ep_kernels.cu -------------------------------------------------------------------------
 constexpr int kMaxEpBins = 12288;  // (chunk, rank) counters of ep_dest_groups (48 KB smem)
 int launch_ep_dest_groups(const uint32_t* idx, int64_t T, int k, int E, int G,

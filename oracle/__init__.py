@@ -44,6 +44,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_route_prep.restype = None
         L.oracle_moe_forward.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, P]
         L.oracle_moe_forward.restype = I
+        L.oracle_moe_forward_ex.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, P, P]
+        L.oracle_moe_forward_ex.restype = I
         L.oracle_activation.argtypes = [F, I]
         L.oracle_activation.restype = F
         L.oracle_num_threads.argtypes = []
@@ -152,13 +154,15 @@ def route_prep(indices: np.ndarray, weights: np.ndarray, num_experts: int):
 # ---------------------------------------------------------------------------------------------
 
 def moe_forward(x, gate, up, down, routing_weights, indices, *, activation: int, moe_type: int,
-                dtype: str, round_dtype: str | None = None, nthreads: int = 0) -> np.ndarray:
+                dtype: str, round_dtype: str | None = None, nthreads: int = 0,
+                with_max_contrib: bool = False):
     """Restates the reference's fused MoE forward (see oracle/oracle.c).
 
     x/gate/up/down are raw storage of `dtype` (uint16 bits for bf16/f16).  Returns the f32 output
     [T,H] before the final rounding to `dtype`.  round_dtype defaults to `dtype` for bf16/f16 (the
     reference's GEMM path rounds the intermediate and each weighted contribution) and to none
-    for f32."""
+    for f32.  with_max_contrib: returns (out, max_contrib), max_contrib [T,H] the largest
+    |rounded weighted contribution| among each token's slots."""
     x = np.ascontiguousarray(x)
     T, H = x.shape
     E, H2, I = gate.shape
@@ -167,18 +171,19 @@ def moe_forward(x, gate, up, down, routing_weights, indices, *, activation: int,
     if round_dtype is None:
         round_dtype = dtype
     out = np.empty((T, H), np.float32)
+    mc = np.empty((T, H), np.float32) if with_max_contrib else None
     if T == 0:
-        return out
-    rc = lib().oracle_moe_forward(
+        return (out, mc) if with_max_contrib else out
+    rc = lib().oracle_moe_forward_ex(
         _ptr(x), _ptr(np.ascontiguousarray(gate)), _ptr(np.ascontiguousarray(up)),
         _ptr(None if down is None else np.ascontiguousarray(down)),
         _ptr(np.ascontiguousarray(routing_weights, dtype=np.float32)),
         _ptr(np.ascontiguousarray(indices).view(np.uint32)),
         T, H, I, E, k, activation, moe_type, DTYPE_CODES[dtype], DTYPE_CODES[round_dtype],
-        nthreads, _ptr(out))
+        nthreads, _ptr(out), _ptr(mc))
     if rc != 0:
         raise MemoryError("oracle_moe_forward: allocation failed")
-    return out
+    return (out, mc) if with_max_contrib else out
 
 
 def activation(x: float, act: int) -> float:

@@ -300,10 +300,13 @@ EXPORT float oracle_activation(float x, int act) { return act_f32(x, act); }
  * to that type, as the reference's f16/bf16 GEMM path does (nomic_moe.cu:374, qwen3_moe.cu:493,
  * qwen3_moe.cu:637-641).  All products accumulate in f32.
  */
-EXPORT int oracle_moe_forward(const void* x, const void* gate, const void* up, const void* down,
-                              const float* routing_w, const uint32_t* indices, int T, int H, int I,
-                              int E, int k, int act, int moe_type, int dtype, int round_dtype,
-                              int nthreads, float* out) {
+/* max_contrib (may be NULL): [T,H] largest |weighted contribution| among each token's slots,
+ * after rounding -- the scale of the rounding steps the result is built from, which the tests use
+ * to tell a one-unit rounding disagreement in a contribution from a wrong result. */
+EXPORT int oracle_moe_forward_ex(const void* x, const void* gate, const void* up, const void* down,
+                                 const float* routing_w, const uint32_t* indices, int T, int H,
+                                 int I, int E, int k, int act, int moe_type, int dtype,
+                                 int round_dtype, int nthreads, float* out, float* max_contrib) {
     int64_t rows = (int64_t)T * k;
     int32_t* offsets = (int32_t*)malloc(sizeof(int32_t) * ((size_t)E + 2));
     int32_t* sflat = (int32_t*)malloc(sizeof(int32_t) * (size_t)(rows > 0 ? rows : 1));
@@ -424,10 +427,26 @@ EXPORT int oracle_moe_forward(const void* x, const void* gate, const void* up, c
             const float* c = contrib + ((size_t)t * k + j) * H;
             for (int n = 0; n < H; ++n) o[n] += c[n];
         }
+        if (max_contrib) {
+            float* mc = max_contrib + (size_t)t * H;
+            for (int n = 0; n < H; ++n) mc[n] = 0.f;
+            for (int j = 0; j < k; ++j) {
+                const float* c = contrib + ((size_t)t * k + j) * H;
+                for (int n = 0; n < H; ++n) mc[n] = fmaxf(mc[n], fabsf(c[n]));
+            }
+        }
     }
     free(item_e); free(item_r);
     free(offsets); free(sflat); free(sw); free(contrib);
     return 0;
+}
+
+EXPORT int oracle_moe_forward(const void* x, const void* gate, const void* up, const void* down,
+                              const float* routing_w, const uint32_t* indices, int T, int H, int I,
+                              int E, int k, int act, int moe_type, int dtype, int round_dtype,
+                              int nthreads, float* out) {
+    return oracle_moe_forward_ex(x, gate, up, down, routing_w, indices, T, H, I, E, k, act,
+                                 moe_type, dtype, round_dtype, nthreads, out, NULL);
 }
 
 EXPORT int oracle_num_threads(void) {
