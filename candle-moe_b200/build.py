@@ -22,8 +22,8 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                  "-I", os.path.join(ROOT, "include"), "-I", CSRC]
-EXTRA = {"router.cu": ["--use_fast_math"]}
-SOURCES = ["router.cu", "route_prep.cu", "moe_simt.cu", "moe_sm100.cu", "moe_sm100_pair.cu",
+EXTRA = {"router.cu": ["--use_fast_math"], "router_proj.cu": ["--use_fast_math"]}
+SOURCES = ["router.cu", "router_proj.cu", "route_prep.cu", "moe_simt.cu", "moe_sm100.cu", "moe_sm100_pair.cu",
            "moe_decode.cu", "ep_kernels.cu", "peer.cu", "capi.cu"]
 
 

@@ -59,6 +59,8 @@ def lib() -> ctypes.CDLL:
         L.moe_status_string.restype = ctypes.c_char_p
         L.moe_topk_softmax_v2.argtypes = [P, P, P, P, I32, I64, I32, I32, P]
         L.moe_topk_softmax_v2.restype = ctypes.c_int
+        L.moe_router_project_topk.argtypes = [P, P, I64, I32, I32, I32, I32, U32, P, P, P, P, P]
+        L.moe_router_project_topk.restype = ctypes.c_int
         L.moe_route_prep.argtypes = [P, P, I64, I32, I32, P, P, P, P]
         L.moe_route_prep.restype = ctypes.c_int
         L.moe_fused_workspace_size.argtypes = [I64, I32, I32, I32, I32, U32, U32]
@@ -221,6 +223,36 @@ def topk_softmax(gating_output: torch.Tensor, top_k: int, renormalize: bool = Fa
     if st != MOE_OK:
         raise MoeError(st, "moe_topk_softmax_v2")
     return w, idx, src
+
+
+def router_project_topk(hidden: torch.Tensor, gate_proj: torch.Tensor, top_k: int,
+                        renormalize: bool = False, return_logits: bool = False):
+    """Router logits = hidden . gate_proj^T fused with topk_softmax (the reference's caller
+    computes the logits with a Linear first, README.md:67-73).  hidden [T,H] and gate_proj [E,H]
+    f16/bf16.  Returns (weights [T,k] f32, indices [T,k] int32, token_expert_indices [T,k]
+    int32), plus the f32 logits [T,E] with return_logits."""
+    for t, n in ((hidden, "hidden"), (gate_proj, "gate_proj")):
+        _need_cuda(t, n)
+        _need_contig(t, n)
+    if hidden.dim() != 2 or gate_proj.dim() != 2 or gate_proj.shape[1] != hidden.shape[1]:
+        raise ValueError("hidden must be [T, H] and gate_proj [E, H]")
+    if gate_proj.dtype != hidden.dtype:
+        raise TypeError("gate_proj must have hidden's dtype")
+    T, H = hidden.shape
+    E = gate_proj.shape[0]
+    dev = hidden.device
+    w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    src = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    logits = torch.empty((T, E), dtype=torch.float32, device=dev) if return_logits else None
+    with torch.cuda.device(dev):
+        st = lib().moe_router_project_topk(_ptr(hidden), _ptr(gate_proj), T, H, E, top_k,
+                                           int(renormalize), fused_moe_internal_dtype(hidden.dtype),
+                                           _ptr(w), _ptr(idx), _ptr(src), _ptr(logits),
+                                           _stream(dev))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_router_project_topk")
+    return (w, idx, src, logits) if return_logits else (w, idx, src)
 
 
 # ---------------------------------------------------------------------------------------------

@@ -97,7 +97,8 @@ int init_device(int dev, DeviceState** out) {
     if (cudaMalloc(&d.err_word, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     const bool attrs_ok = route_prep_set_attributes() && sm100_set_attributes() &&
-                          sm100_pair_set_attributes() && decode_set_attributes();
+                          sm100_pair_set_attributes() && decode_set_attributes() &&
+                          router_project_set_attributes();
     cudaGetLastError();  // attribute failures are reported here, not by a later call
     if (!attrs_ok) return MOE_ERR_CUDA;
     d.max_pairs = sm100_pair_max_clusters();
@@ -542,6 +543,52 @@ CMOE_API int moe_topk_softmax_v2(const float* gating_output, float* topk_weights
   if (launch_router(gating_output, topk_weights, topk_indices, token_expert_indices, num_experts,
                     static_cast<int>(num_tokens), topk, renormalize, ds->num_sms,
                     static_cast<cudaStream_t>(stream)) != 0)
+    return MOE_ERR_UNSUPPORTED;
+  ++g_launches;
+  return finish(MOE_OK);
+}
+
+CMOE_API int moe_router_project_topk(const void* input, const void* gate_proj,
+                                     int64_t num_tokens, int32_t hidden_dim, int32_t num_experts,
+                                     int32_t topk, int32_t renormalize, uint32_t dtype,
+                                     float* topk_weights, int32_t* topk_indices,
+                                     int32_t* token_expert_indices, float* logits, void* stream) {
+  if (num_tokens < 0 || hidden_dim <= 0 || num_experts <= 0 || topk <= 0 || dtype > 2)
+    return MOE_ERR_INVALID_ARG;
+  if (num_tokens == 0) return MOE_OK;
+  if (!input || !gate_proj || !topk_weights || !topk_indices || !token_expert_indices)
+    return MOE_ERR_INVALID_ARG;
+  if (dtype == kF32 || (num_experts & (num_experts - 1)) != 0 || num_experts > 256 ||
+      topk > num_experts || topk > router_project_max_k() || hidden_dim % 64 != 0 ||
+      num_tokens > INT32_MAX / num_experts || !aligned16(input) || !aligned16(gate_proj))
+    return MOE_ERR_UNSUPPORTED;
+  DeviceState* ds = nullptr;
+  int st = current_device_state(&ds);
+  if (st != MOE_OK) return st;
+  if (ds->cc_major != 10 || !g_encode) return MOE_ERR_UNSUPPORTED;
+  // x [T, H] in 64 x 128-row boxes; W_r [E, H] in 64 x max(E, 16)-row boxes (rows past E are
+  // outside the tensor: the TMA fills them with zeros)
+  CUtensorMap mx, mw;
+  const int n_box = num_experts < 16 ? 16 : num_experts;
+  if (!make_map_2d(&mx, static_cast<int>(dtype), input, hidden_dim,
+                   static_cast<uint64_t>(num_tokens), 64, 128) ||
+      !make_map_2d(&mw, static_cast<int>(dtype), gate_proj, hidden_dim, num_experts, 64, n_box))
+    return MOE_ERR_CUDA;
+  RouterProjParams p;
+  p.out_w = topk_weights;
+  p.out_idx = topk_indices;
+  p.out_src = token_expert_indices;
+  p.logits = logits;
+  p.err = ds->err_word;
+  p.num_tokens = static_cast<int>(num_tokens);
+  p.H = hidden_dim;
+  p.k = topk;
+  p.renorm = renormalize;
+  const int64_t tiles = (num_tokens + 127) / 128;
+  const int sms = ds->num_sms;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  if (launch_router_project(static_cast<int>(dtype), num_experts, mx, mw, p, grid,
+                            static_cast<cudaStream_t>(stream)) != 0)
     return MOE_ERR_UNSUPPORTED;
   ++g_launches;
   return finish(MOE_OK);

@@ -16,6 +16,20 @@ void add_launches(int64_t n);
 int launch_router(const float* logits, float* w, int32_t* idx, int32_t* src, int num_experts,
                   int num_tokens, int k, int renorm, int num_sms, cudaStream_t stream);
 
+// ---- router_proj.cu (R0: gate projection fused with the softmax + top-k) ---------------------
+struct RouterProjParams {
+  float* out_w;          // [T, k]
+  int32_t* out_idx;      // [T, k]
+  int32_t* out_src;      // [T, k] = j*T + t
+  float* logits;         // [T, E] f32 copy of the logits, or null
+  uint32_t* err;         // device error word
+  int num_tokens, H, k, renorm;
+};
+int router_project_max_k();
+bool router_project_set_attributes();
+int launch_router_project(int dtype, int E, const CUtensorMap& x, const CUtensorMap& w,
+                          const RouterProjParams& p, int grid, cudaStream_t s);
+
 // ---- route_prep.cu ---------------------------------------------------------------------------
 size_t route_prep_scratch_bytes(int64_t rows, int E);
 int route_prep_max_experts();

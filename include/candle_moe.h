@@ -89,6 +89,26 @@ int moe_topk_softmax_v2(const float* gating_output, float* topk_weights, int32_t
                         int32_t topk, int32_t renormalize, void* stream);
 
 /*
+ * The router's gate projection fused with the softmax + top-k (no counterpart in the reference,
+ * whose caller computes the logits with a Linear layer and passes them to topk_softmax,
+ * README.md:67-73): logits = input . gate_proj^T on the tensor cores, then topk_softmax's picks
+ * and weights (optionally renormalised as moe_topk_softmax_v2 does), without writing the
+ * logits to memory.
+ *   input          [num_tokens, hidden_dim] f16/bf16 (dtype 0/1), 16-byte aligned
+ *   gate_proj      [num_experts, hidden_dim] same dtype (the Linear's weight), 16-byte aligned
+ *   topk_weights, topk_indices, token_expert_indices: as topk_softmax
+ *   logits         [num_tokens, num_experts] f32 out: the logits the picks were made from, or
+ *                  NULL (for checking: topk_softmax on them gives the same picks and weights)
+ * num_experts a power of two <= 256, topk <= min(num_experts, 16), hidden_dim a multiple of 64;
+ * otherwise MOE_ERR_UNSUPPORTED.
+ */
+int moe_router_project_topk(const void* input, const void* gate_proj, int64_t num_tokens,
+                            int32_t hidden_dim, int32_t num_experts, int32_t topk,
+                            int32_t renormalize, uint32_t dtype, float* topk_weights,
+                            int32_t* topk_indices, int32_t* token_expert_indices, float* logits,
+                            void* stream);
+
+/*
  * Sort / align step on its own.  Replaces launch_preprocessing (kernels/preprocessing.cuh:253-313),
  * which the reference runs inside fused_moe without exporting it.
  *   expert_offsets    [num_experts + 2] i32 out: exclusive prefix of per-expert row counts,
