@@ -443,6 +443,7 @@ def run_ours(args, world, rank, local):
         # microseconds and config 4's decode step (8 tokens)
         line["router_c1"] = measure_router_c1()
         line["decode_c4_t8"] = measure_decode_c4(8)
+        line["router_projection_c5"] = measure_router_projection_c5()
     if ep:
         # non-zero when an arrival wait of the exchange ran out (a rank never signalled)
         line["device_error_bits"] = int(max_over_ranks(world,
@@ -535,6 +536,41 @@ def measure_decode_c4(tokens=8, dtype="bf16"):
             "peak_kind": f"{kind} HBM copy", "gemm_path": candle_moe.last_gemm_path(),
             "timing": "CUDA-graph replay, 10 steps per graph x 40 replays, CUDA events",
             "gpu_launches_per_step": launches}
+
+
+def measure_router_projection_c5():
+    """The router's gate projection at config 5's shape (65536 tokens, H 2048, 128 experts,
+    top-8, renormalised): the fused kernel (moe_router_project_topk) against the two-step path a
+    model runs without it -- the Linear (torch, cuBLAS) to bf16 logits, cast to f32, then
+    topk_softmax.  Device microseconds per call, CUDA-graph replay.  The fused kernel is bound
+    by reading the hidden states once: T*H*2 + E*H*2 + T*k*12 bytes."""
+    import torch
+    import candle_moe
+    T, H, E, k = 65536, 2048, 128, 8
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(E, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    fused_us, fused_launches = _graph_time_us(
+        lambda: candle_moe.router_project_topk(x, w, k, renormalize=True), 20, 5)
+
+    def two_step():
+        logits = torch.nn.functional.linear(x, w).float()
+        return candle_moe.topk_softmax(logits, k, renormalize=True)
+
+    two_us, _ = _graph_time_us(two_step, 20, 5)
+    nbytes = T * H * 2 + E * H * 2 + T * k * 12
+    peaks, kind = load_peaks()
+    del x, w
+    torch.cuda.empty_cache()
+    return {"fused_us": fused_us, "two_step_us": two_us, "speedup": two_us / fused_us,
+            "tokens": T, "hidden": H, "experts": E, "top_k": k, "bytes_per_call": nbytes,
+            "fused_gb_per_s": nbytes / (fused_us * 1e-6) / 1e9,
+            "fused_hbm_frac": nbytes / (fused_us * 1e-6) / 1e9 / peaks["hbm_gbs"],
+            "peak_kind": f"{kind} HBM copy",
+            "two_step": "torch linear (cuBLAS) to bf16 logits, .float(), topk_softmax",
+            "timing": "CUDA-graph replay, 5 calls per graph x 20 replays, CUDA events",
+            "gpu_launches_per_call": fused_launches}
 
 
 def cpu_baseline(cfg, inp, target_s=10.0):

@@ -575,6 +575,57 @@ class FusedMoE:
                          self.activation.to_int(), moe_type)
 
 
+class SparseMoeBlock:
+    """The MoE layer a model calls around this library (the router Linear, the softmax top-k and
+    the expert FFN of README.md:61-97, as in Qwen3-MoE's and Qwen2-MoE's sparse blocks).
+
+    forward(hidden [T,H]) = the router projection fused with the softmax + top-k
+    (router_project_topk, renormalised when norm_topk_prob), then the routed experts
+    (FusedMoE.forward), plus -- when shared-expert weights are given -- a shared expert that
+    every token goes through (FusedMoE with one expert and k = 1, weighted by
+    sigmoid(hidden . shared_expert_gate^T) when that gate is given, else by 1).
+
+    router_weight [E,H]; gate/up [E,H,I]; down [E,I,H] (Qwen3, moe_type 0) or None (Nomic,
+    moe_type 1); shared_gate/shared_up [1,H,Is] and shared_down [1,Is,H]; shared_expert_gate
+    [1,H].  All in the hidden states' dtype (f16/bf16)."""
+
+    def __init__(self, router_weight, gate_weights, up_weights, down_weights, top_k: int,
+                 activation: Activation = Activation.Silu, norm_topk_prob: bool = True,
+                 shared_gate=None, shared_up=None, shared_down=None, shared_expert_gate=None):
+        self.router_weight = router_weight
+        self.gate_weights, self.up_weights, self.down_weights = gate_weights, up_weights, down_weights
+        self.moe_type = 0 if down_weights is not None else 1
+        self.num_experts = router_weight.shape[0]
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.experts = FusedMoE(self.num_experts, top_k, activation)
+        self.shared = None
+        if shared_gate is not None:
+            if shared_up is None or (self.moe_type == 0 and shared_down is None):
+                raise ValueError("a shared expert needs gate, up (and down for moe_type 0)")
+            self.shared = (shared_gate, shared_up, shared_down)
+            self.shared_moe = FusedMoE(1, 1, activation)
+        self.shared_expert_gate = shared_expert_gate
+
+    def forward(self, hidden: torch.Tensor, return_router_logits: bool = False):
+        w, idx, _, logits = router_project_topk(hidden, self.router_weight, self.top_k,
+                                                renormalize=self.norm_topk_prob,
+                                                return_logits=True)
+        out = self.experts.forward(hidden, self.gate_weights, self.up_weights, self.down_weights,
+                                   w, idx, self.moe_type)
+        if self.shared is not None:
+            T = hidden.shape[0]
+            if self.shared_expert_gate is not None:
+                sw = torch.sigmoid(torch.nn.functional.linear(
+                    hidden, self.shared_expert_gate).float()).contiguous()
+            else:
+                sw = torch.ones((T, 1), dtype=torch.float32, device=hidden.device)
+            sidx = torch.zeros((T, 1), dtype=torch.int32, device=hidden.device)
+            g, u, d = self.shared
+            out = out + self.shared_moe.forward(hidden, g, u, d, sw, sidx, self.moe_type)
+        return (out, logits) if return_router_logits else out
+
+
 def device_error_bits(device: int = 0, clear: bool = False) -> int:
     return int(lib().moe_device_error_bits(device, int(clear)))
 

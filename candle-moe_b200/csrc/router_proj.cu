@@ -30,7 +30,7 @@ namespace cmoe {
 constexpr int kRpThreads = 256;
 constexpr int kRpBM = 128;   // tokens per tile
 constexpr int kRpBK = 64;    // hidden elements per stage
-constexpr int kRpRingBytes = 192 * 1024;
+constexpr int kRpRingBytes = 220 * 1024;  // operand ring (+ staging, see kWarpPick)
 constexpr int kRpMaxK = 16;
 
 // R1's lane geometry for E experts (RouterGeom in router.cu).
@@ -45,10 +45,24 @@ struct RpGeom {
   static constexpr int kABytes = kRpBM * kRpBK * 2;    // 16 KB
   static constexpr int kBBytes = (kN * 128 + 1023) / 1024 * 1024;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kRpRingBytes / kStageBytes > 8 ? 8 : kRpRingBytes / kStageBytes;
+  // E = 64 / 128 pick per warp from probabilities staged in shared memory (4 warps x 16 rows
+  // x (E + 1) floats), which takes room from the operand ring
+  static constexpr bool kWarpPick = E == 64 || E == 128;
+  static constexpr int kStageFloats = kWarpPick ? 4 * 16 * (E + 1) : 0;
+  static constexpr int kRing = kRpRingBytes - (kWarpPick ? (kStageFloats * 4 + 1023) / 1024 * 1024 : 0);
+  static constexpr int kStages = kRing / kStageBytes > 8 ? 8 : kRing / kStageBytes;
   static constexpr int kTmemCols = 2 * kN <= 32 ? 32 : 2 * kN <= 64 ? 64 : 2 * kN <= 128 ? 128
                                  : 2 * kN <= 256 ? 256 : 512;
 };
+
+// order-preserving 32-bit keys of non-NaN floats (as router.cu's order_key / from_order_key)
+__device__ __forceinline__ uint32_t rp_order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float rp_from_order_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
 template <typename T> struct RpFmt;
 template <> struct RpFmt<__half> { static constexpr uint32_t v = 0; };
@@ -90,6 +104,11 @@ __global__ void __launch_bounds__(kRpThreads, 1)
   __shared__ int s_abort;
 
   const uint32_t smem_base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  // E = 64 and 128: the probabilities of 16 rows per epilogue warp, after the operand ring
+  constexpr bool kWarpPick = RpGeom<E>::kWarpPick;
+  float* s_stage = reinterpret_cast<float*>(smem_raw + (smem_base - smem_addr(smem_raw)) +
+                                            static_cast<size_t>(RpGeom<E>::kStages) *
+                                                RpGeom<E>::kStageBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int k = KC > 0 ? KC : p.k;
@@ -216,7 +235,7 @@ __global__ void __launch_bounds__(kRpThreads, 1)
       float part[Gm::kTpr];
 #pragma unroll
       for (int g = 0; g < Gm::kTpr; ++g) part[g] = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int cb = 0; cb < kChunks; ++cb) {
         float v[kCh];
         rp_load_chunk<E, kCh>(tb, cb * kCh, v);
@@ -225,10 +244,8 @@ __global__ void __launch_bounds__(kRpThreads, 1)
           const int c = cb * kCh + i;
           if (c < E) {
             // column c belongs to R1 lane (c / ELTS) % TPR; its (l, i) order is column order
-            const int g = (c / Gm::kElts) % Gm::kTpr;
-#pragma unroll
-            for (int gg = 0; gg < Gm::kTpr; ++gg)
-              if (gg == g) part[gg] += expf(v[i] - m);
+            // (c is a compile-time index here, so part[] stays in registers)
+            part[(c / Gm::kElts) % Gm::kTpr] += expf(v[i] - m);
           }
         }
       }
@@ -243,14 +260,133 @@ __global__ void __launch_bounds__(kRpThreads, 1)
           }
       }
       const float rs = 1.f / part[0];
-      // pass 3: the k largest probabilities, ties to the lower expert (kept sorted)
-      float bw[kRpMaxK];
-      int be[kRpMaxK];
+      if (kWarpPick) {
+        // pass 3 (E = 64, 128): the probabilities go through shared memory (16 of this warp's
+        // rows at a time, row stride E + 1 floats: conflict-free both ways), then the warp picks
+        // as R1 does when a warp owns a row -- each lane sorts its E/32 values (columns lane +
+        // 32 l) by (value desc, expert asc), and every pick is a warp max over the lanes' heads
+        // (as order-preserving keys) and a warp min over the experts at that max; eight rows
+        // are picked side by side so that their reduction chains overlap.
+        float* st = s_stage + static_cast<size_t>(q) * 16 * (E + 1);
+        constexpr int kPer = E >= 32 ? E / 32 : 1;  // values per lane
+        constexpr int kRows = 8;  // rows picked side by side: independent reduction chains
+        const int64_t row0 = static_cast<int64_t>(tile) * kRpBM + q * 32;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          // lanes 16h..16h+15 stage their rows' probabilities (row stride E + 1 floats); the
+          // TMEM loads are warp-wide (.sync.aligned), only the stores are per half
+          const bool mine = (lane >> 4) == h;
+#pragma unroll 1
+          for (int cb = 0; cb < kChunks; ++cb) {
+            float v[kCh];
+            rp_load_chunk<E, kCh>(tb, cb * kCh, v);
+            if (mine) {
 #pragma unroll
-      for (int j = 0; j < kRpMaxK; ++j) {
+              for (int i = 0; i < kCh; ++i)
+                st[(lane & 15) * (E + 1) + cb * kCh + i] = expf(v[i] - m) * rs;
+            }
+          }
+          if (h == 1) {
+            // every probability is out of TMEM: release the accumulator
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(&bar_acce[buf]));
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int r0 = 0; r0 < 16; r0 += kRows) {
+            uint32_t key[kRows][kPer];
+            int id[kRows][kPer];
+#pragma unroll
+            for (int rr = 0; rr < kRows; ++rr) {
+#pragma unroll
+              for (int l = 0; l < kPer; ++l) {
+                key[rr][l] = rp_order_key(st[(r0 + rr) * (E + 1) + lane + 32 * l]);
+                id[rr][l] = lane + 32 * l;
+              }
+              // odd-even transposition sort of this lane's values: (value desc, expert asc)
+#pragma unroll
+              for (int t = 0; t < kPer; ++t) {
+#pragma unroll
+                for (int a = t & 1; a + 1 < kPer; a += 2) {
+                  const bool sw = key[rr][a + 1] > key[rr][a] ||
+                                  (key[rr][a + 1] == key[rr][a] && id[rr][a + 1] < id[rr][a]);
+                  const uint32_t ka = key[rr][a], kb2 = key[rr][a + 1];
+                  const int ia = id[rr][a], ib = id[rr][a + 1];
+                  key[rr][a] = sw ? kb2 : ka;
+                  key[rr][a + 1] = sw ? ka : kb2;
+                  id[rr][a] = sw ? ib : ia;
+                  id[rr][a + 1] = sw ? ia : ib;
+                }
+              }
+            }
+            float mine_w[kRows], wsum[kRows];
+            int mine_e[kRows];
+#pragma unroll
+            for (int rr = 0; rr < kRows; ++rr) {
+              mine_w[rr] = 0.f;
+              wsum[rr] = 0.f;
+              mine_e[rr] = 0;
+            }
+#pragma unroll 1
+            for (int j = 0; j < k; ++j) {
+              uint32_t km[kRows];
+#pragma unroll
+              for (int rr = 0; rr < kRows; ++rr) km[rr] = __reduce_max_sync(0xffffffffu, key[rr][0]);
+              int be[kRows];
+#pragma unroll
+              for (int rr = 0; rr < kRows; ++rr)
+                be[rr] = static_cast<int>(__reduce_min_sync(
+                    0xffffffffu,
+                    key[rr][0] == km[rr] ? static_cast<uint32_t>(id[rr][0]) : 0xffffffffu));
+#pragma unroll
+              for (int rr = 0; rr < kRows; ++rr) {
+                if (id[rr][0] == be[rr]) {  // this lane held the pick: pop it
+#pragma unroll
+                  for (int l = 0; l + 1 < kPer; ++l) {
+                    key[rr][l] = key[rr][l + 1];
+                    id[rr][l] = id[rr][l + 1];
+                  }
+                  key[rr][kPer - 1] = 0u;
+                  id[rr][kPer - 1] = 0x7fffffff;
+                }
+                const float wv = rp_from_order_key(km[rr]);
+                wsum[rr] += wv;
+                if (lane == j) {
+                  mine_w[rr] = wv;
+                  mine_e[rr] = be[rr];
+                }
+              }
+            }
+#pragma unroll
+            for (int rr = 0; rr < kRows; ++rr) {
+              const int64_t rrow = row0 + 16 * h + r0 + rr;
+              if (lane < k && rrow < p.num_tokens) {
+                const int64_t o = rrow * k + lane;
+                p.out_w[o] = p.renorm ? mine_w[rr] / wsum[rr] : mine_w[rr];
+                p.out_idx[o] = mine_e[rr];
+                p.out_src[o] =
+                    static_cast<int32_t>(static_cast<int64_t>(lane) * p.num_tokens + rrow);
+              }
+            }
+          }
+          __syncwarp();
+        }
+        __syncwarp();
+        continue;
+      }
+      // pass 3 (E <= 32 or 256): the k largest probabilities, ties to the lower expert, kept
+      // sorted; a value enters only when strictly larger than the k-th (columns arrive in
+      // ascending order, so an equal later value loses, as in R1)
+      constexpr int KK = KC > 0 ? KC : kRpMaxK;
+      float bw[KK];
+      int be[KK];
+#pragma unroll
+      for (int j = 0; j < KK; ++j) {
         bw[j] = -INFINITY;
         be[j] = 0x7fffffff;
       }
+      float thr = -INFINITY;  // the k-th largest so far
 #pragma unroll 1
       for (int cb = 0; cb < kChunks; ++cb) {
         float v[kCh];
@@ -261,17 +397,21 @@ __global__ void __launch_bounds__(kRpThreads, 1)
           if (c < E) {
             float pv = expf(v[i] - m) * rs;
             int pe = c;
-            // insert (pv, c) into the sorted list: a later column wins only by a larger value
+            if (pv > thr) {
 #pragma unroll
-            for (int j = 0; j < (KC > 0 ? KC : kRpMaxK); ++j) {
-              if (j < k && pv > bw[j]) {
-                const float tw = bw[j];
-                const int te = be[j];
-                bw[j] = pv;
-                be[j] = pe;
-                pv = tw;
-                pe = te;
+              for (int j = 0; j < KK; ++j) {
+                if (j < k && pv > bw[j]) {
+                  const float tw = bw[j];
+                  const int te = be[j];
+                  bw[j] = pv;
+                  be[j] = pe;
+                  pv = tw;
+                  pe = te;
+                }
               }
+#pragma unroll
+              for (int j = 0; j < KK; ++j)
+                if (j == k - 1) thr = bw[j];
             }
           }
         }
@@ -282,10 +422,10 @@ __global__ void __launch_bounds__(kRpThreads, 1)
       if (live) {
         float wsum = 0.f;
 #pragma unroll
-        for (int j = 0; j < (KC > 0 ? KC : kRpMaxK); ++j)
+        for (int j = 0; j < KK; ++j)
           if (j < k) wsum += bw[j];
 #pragma unroll
-        for (int j = 0; j < (KC > 0 ? KC : kRpMaxK); ++j) {
+        for (int j = 0; j < KK; ++j) {
           if (j < k) {
             const int64_t o = row * k + j;
             p.out_w[o] = p.renorm ? bw[j] / wsum : bw[j];
@@ -315,7 +455,8 @@ int router_project_max_k() { return kRpMaxK; }
 
 template <typename T, int E, int KC>
 static size_t rp_smem() {
-  return static_cast<size_t>(RpGeom<E>::kStages) * RpGeom<E>::kStageBytes + 1024;
+  return static_cast<size_t>(RpGeom<E>::kStages) * RpGeom<E>::kStageBytes + 1024 +
+         static_cast<size_t>(RpGeom<E>::kStageFloats) * sizeof(float);
 }
 
 template <typename T, int E, int KC>
