@@ -215,7 +215,8 @@ def run_ours(args, world, rank, local):
     if ep:
         import expert_parallel
         layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act),
-                                                  mode=args.ep_mode, transport=args.ep_transport)
+                                                  mode=args.ep_mode, transport=args.ep_transport,
+                                                  chunks=args.ep_chunks)
         if args.sm_reserve >= 0:
             layer.sm_reserve = args.sm_reserve
         inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
@@ -444,13 +445,55 @@ def run_ours(args, world, rank, local):
         line["router_c1"] = measure_router_c1()
         line["decode_c4_t8"] = measure_decode_c4(8)
         line["router_projection_c5"] = measure_router_projection_c5()
+    failed = False
     if ep:
-        # non-zero when an arrival wait of the exchange ran out (a rank never signalled)
-        line["device_error_bits"] = int(max_over_ranks(world,
-                                                       candle_moe.device_error_bits(local)))
+        if not args.no_extra:
+            line["strong_scaling"] = measure_ep_strong(args, world, inp, layer, renorm, k,
+                                                       moe_type, T)
+        # non-zero when an arrival wait of the exchange ran out (a rank never signalled): the
+        # step's output is incomplete, so the run fails after its line is printed
+        bits = int(max_over_ranks(world, candle_moe.device_error_bits(local)))
+        line["device_error_bits"] = bits
+        failed = bits != 0
         layer.close()
     if rank == 0:
         emit(line)
+    if failed:
+        raise SystemExit("expert-parallel exchange: an arrival wait ran out "
+                         f"(device error bits {bits:#x})")
+
+
+def measure_ep_strong(args, world, inp, layer, renorm, k, moe_type, T):
+    """Strong scaling of the expert-parallel layer: BASELINE config 5's 65536 tokens split
+    across the ranks (T / N each; the weak-scaling headline keeps T per rank).  Same timing
+    rules: warm-up, barrier + synchronize around the timed steps, max over ranks."""
+    import torch
+    import candle_moe
+    Ts = T // world
+    logits = inp["logits"][:Ts].contiguous()
+    x = inp["x"][:Ts].contiguous()
+
+    def step():
+        w, idx, _ = candle_moe.topk_softmax(logits, k, renormalize=renorm)
+        return layer.forward(x, inp["gate"], inp["up"], inp["down"], w, idx, moe_type)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
+    return {"tokens_total": Ts * world, "tokens_per_rank": Ts, "ms_per_step": ms,
+            "value": Ts * world / (ms / 1e3), "unit": "tokens/s",
+            "note": "BASELINE config 5's 65536 tokens split across the ranks (strong scaling)"}
 
 
 def _graph_time_us(fn, reps, per_graph):
@@ -681,6 +724,8 @@ def main():
                     help="expert-parallel row exchange into peer-mapped landing buffers by SM "
                          "stores fused with pack / slot sum (push) or by copy engines (copy), "
                          "or NCCL all_to_all_single (collective)")
+    ap.add_argument("--ep-chunks", type=int, default=4,
+                    help="expert-parallel token chunks pipelined through dispatch/compute/return")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
     ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3, 4],

@@ -315,6 +315,7 @@ def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="
         diff = float((o - r_).abs().max()) / rms
         stats = {k_: int(v) for k_, v in layer.last_stats.items()}
         stats["error_bits"] = candle_moe.device_error_bits(rank)
+        layer.check_errors()  # raises if an arrival wait ran out
         layer.close()
         result_q.put((rank, same and stats["error_bits"] == 0, diff, stats))
     finally:
