@@ -728,10 +728,11 @@ def main():
                     help="expert-parallel token chunks pipelined through dispatch/compute/return")
     ap.add_argument("--sm-reserve", type=int, default=-1,
                     help="SMs the GEMMs leave to the NCCL exchange (expert parallel; -1 = default)")
-    ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3, 4],
+    ap.add_argument("--gemm-path", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6],
                     help="expert GEMM family: 0 automatic, 1 SIMT, 2 tensor cores, 3 "
-                         "automatic with one-CTA tensor-core kernels only, 4 automatic with "
-                         "GEMM-1 on CTA pairs too (experimental)")
+                         "automatic without CTA pairs, 4 automatic with GEMM-1 on CTA pairs too "
+                         "(experimental), 5 automatic without the decode kernels, 6 decode "
+                         "kernels at any size")
     ap.add_argument("--tokens", type=int, default=0,
                     help="override the token count (small profiling cases)")
     args = ap.parse_args()

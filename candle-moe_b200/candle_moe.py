@@ -631,9 +631,10 @@ def device_error_bits(device: int = 0, clear: bool = False) -> int:
 
 
 def set_gemm_path(path: int) -> int:
-    """0 automatic, 1 SIMT only, 2 tensor cores only, 3 automatic with one-CTA tensor-core
-    kernels only (no CTA pairs), 4 automatic with GEMM-1 on CTA pairs too (experimental);
-    returns the previous setting."""
+    """0 automatic (decode kernels for <= 32 tokens, grouped GEMMs above), 1 SIMT only,
+    2 tensor cores only, 3 automatic without CTA pairs, 4 automatic with GEMM-1 on CTA pairs too
+    and no decode kernels (experimental), 5 automatic without the decode kernels, 6 decode
+    kernels at any token count; returns the previous setting."""
     return int(lib().moe_set_gemm_path(path))
 
 
@@ -646,6 +647,7 @@ def set_sm_reserve(sms: int) -> int:
 
 
 def last_gemm_path() -> int:
+    """Kernels of this thread's last fused call: 1 SIMT, 2 grouped GEMMs, 3 decode kernels."""
     return int(lib().moe_last_gemm_path())
 
 

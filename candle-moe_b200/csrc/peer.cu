@@ -1,11 +1,13 @@
 // Arrival flags of the expert-parallel exchange over peer-mapped memory.
 //
-// Rows travel between GPUs by copy engine (cudaMemcpyAsync into a peer's IPC-mapped landing
-// buffer), so the exchange takes no SM time away from the grouped GEMMs.  Only the arrival
-// signal needs a kernel: after a rank's copies to every peer have completed (stream-ordered
-// behind them), one thread per peer release-stores an epoch number into that peer's flag array,
-// and the receiving rank's compute stream runs a bounded acquire-load wait on its own flags
-// before the kernels that read the rows.  The reference has no multi-GPU path.
+// Rows travel between GPUs into a peer's IPC-mapped landing buffer either by SM stores fused
+// with the kernels that produce them (the default "push" transport: moe_ep_push_pairs and
+// moe_segment_sum_push in ep_kernels.cu, which share the SMs with the grouped GEMMs) or by copy
+// engine (the "copy" transport: cudaMemcpyAsync, no SM time).  Either way the arrival signal is
+// this file's kernel: after a rank's rows to every peer are written (stream-ordered behind
+// them), one thread per peer release-stores an epoch number into that peer's flag array, and the
+// receiving rank's compute stream runs a bounded acquire-load wait on its own flags before the
+// kernels that read the rows.  The reference has no multi-GPU path.
 #include <stdint.h>
 
 #include "common.cuh"

@@ -235,11 +235,14 @@ uint32_t moe_device_error_bits(int32_t device, int32_t clear);
 
 /*
  * Kernel family selection for the f16/bf16 expert GEMMs: 0 = automatic (tensor cores where the
- * shape allows; the Qwen3 GEMM-2 of fused_moe / moe_fused_v2 runs on CTA pairs, cta_group::2 with
- * M = 256, when the hidden size is a multiple of 256), 1 = always the SIMT kernels, 2 = tensor
- * cores only (unsupported shapes then return MOE_ERR_UNSUPPORTED), 3 = as 0 but one-CTA
- * tensor-core kernels only, 4 = as 0 with the Qwen3 GEMM-1 on CTA pairs too (experimental: correct,
- * slower).  Process-wide; returns the previous value (-1 for an unknown path).
+ * shape allows: calls of at most 32 tokens take the decode kernels, weight-streaming with the
+ * combine fused; larger ones the grouped GEMMs, whose Qwen3 GEMM-2 in fused_moe / moe_fused_v2
+ * runs on CTA pairs, cta_group::2 with M = 256, when the hidden size is a multiple of 256),
+ * 1 = always the SIMT kernels, 2 = tensor cores only (unsupported shapes then return
+ * MOE_ERR_UNSUPPORTED), 3 = as 0 but no CTA pairs, 4 = as 0 with the Qwen3 GEMM-1 on CTA pairs
+ * too and no decode kernels (experimental: correct, slower), 5 = as 0 without the decode
+ * kernels, 6 = as 0 with the decode kernels at any token count.  Process-wide; returns the
+ * previous value (-1 for an unknown path).
  */
 int32_t moe_set_gemm_path(int32_t path);
 
@@ -250,8 +253,8 @@ int32_t moe_set_gemm_path(int32_t path);
  */
 int32_t moe_set_sm_reserve(int32_t sms);
 
-/* Which family served the last moe_fused_v2 / fused_moe call of this thread: 1 SIMT, 2 tensor
- * cores, 0 none. */
+/* Which family served the last moe_fused_v2 / fused_moe call of this thread: 1 SIMT, 2 tensor-core
+ * grouped GEMMs, 3 tensor-core decode kernels, 0 none. */
 int32_t moe_last_gemm_path(void);
 
 /*
@@ -288,8 +291,10 @@ int moe_route_prep_noalloc(const uint32_t* expert_indices, const float* routing_
 
 /*
  * Peer-mapped buffers and arrival flags for the expert-parallel exchange over NVLink (no
- * counterpart in the reference, which has no multi-GPU path).  Rows move by copy engine into a
- * peer's landing buffer (moe_copy_async), so the exchange uses no SMs.
+ * counterpart in the reference, which has no multi-GPU path).  Rows move into a peer's landing
+ * buffer either by SM stores fused with the kernels that produce them (moe_ep_push_pairs,
+ * moe_segment_sum_push below: the default "push" transport of expert_parallel.py) or by copy
+ * engine (moe_copy_async: the "copy" transport, no SM time).
  *
  * moe_peer_alloc: device memory on the current device that other processes can map, zero-filled;
  *   writes the pointer and a MOE_PEER_HANDLE_BYTES-byte handle to pass to the other ranks.
