@@ -105,6 +105,17 @@ __device__ __forceinline__ int next_tile_from_ring(uint64_t* tfull, uint64_t* te
   return t;
 }
 
+// The tile id in ring slot `it` without consuming it (the gather warps look one tile ahead to
+// load the next tile's row indices early; next_tile_from_ring later consumes the slot).
+__device__ __forceinline__ int peek_tile_in_ring(uint64_t* tfull, const int* ring, int it,
+                                                 volatile int* abort, uint32_t* err) {
+  const int slot = it % kTileRing;
+  const uint32_t par = static_cast<uint32_t>((it / kTileRing) & 1);
+  bool got = mbar_wait_bounded(smem_addr(&tfull[slot]), par, abort, err, kErrWaitFull);
+  got = __all_sync(0xffffffffu, got);
+  return got ? ring[slot] : -2;
+}
+
 template <typename T, int MODE, int BN>
 __global__ void __launch_bounds__(kSm100Threads, 1)
     sm100_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -175,23 +186,33 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     // ------------------------------------------------------------------ TMA producer (B; A too
     // when A is a contiguous run of sorted rows)
     // Also the tile scheduler: tiles are taken from a global counter (so CTAs that start late
-    // take fewer), and each tile id is published to the other roles through a 4-deep ring.
+    // take fewer), and each tile id is published to the other roles through a 4-deep ring, one
+    // tile ahead of the tile being loaded (the gather warps read the next tile's row indices
+    // while the current tile streams).
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int tile = static_cast<int>(atomicAdd(p.tile_counter, 1u));
-      for (int it = 0; ok; ++it) {
+      auto publish = [&](int it, int t) {
         const int slot = it % kTileRing;
         if (!mbar_wait_bounded(smem_addr(&bar_tempty[slot]),
                                static_cast<uint32_t>((it / kTileRing) & 1) ^ 1u, &s_abort, p.err,
                                kErrWaitEmpty)) {
-          break;
+          return false;
         }
-        if (tile >= total_tiles) tile = -1;
-        s_tile[slot] = tile;
+        s_tile[slot] = t;
         mbar_arrive(smem_addr(&bar_tfull[slot]));
-        if (tile < 0) break;
-        const int next_tile = static_cast<int>(atomicAdd(p.tile_counter, 1u));
+        return true;
+      };
+      // The id after the next one is claimed during the current tile's first k-block, so the
+      // atomic's round trip is not paid at a tile boundary.
+      int tile = static_cast<int>(atomicAdd(p.tile_counter, 1u));
+      if (tile >= total_tiles) tile = -1;
+      int next_tile = tile >= 0 ? static_cast<int>(atomicAdd(p.tile_counter, 1u)) : -1;
+      ok = publish(0, tile);
+      for (int it = 0; ok && tile >= 0; ++it) {
+        if (next_tile >= total_tiles) next_tile = -1;
+        if (!publish(it + 1, next_tile)) break;
+        int after_next = -1;
         const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
@@ -224,8 +245,11 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             stage = 0;
             phase ^= 1u;
           }
+          if (kb == 0 && next_tile >= 0)
+            after_next = static_cast<int>(atomicAdd(p.tile_counter, 1u));
         }
         tile = next_tile;
+        next_tile = after_next;
       }
     }
   } else if (warp == 1) {
@@ -283,6 +307,8 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
     // Thread g copies 16-byte chunk c = g%8 of rows q + 8i (q = g/8, i = 0..15) of each stage,
     // writing them in the 128-byte-swizzled K-major layout the MMA descriptor expects (chunk c of
     // row r lands at chunk c ^ (r % 8) = c ^ q).
+    // The row indices of the next tile are loaded while the current tile streams (its id is
+    // in the ring one tile ahead), so a tile's first copies wait only for the rows themselves.
     if (C::kGather) {
       const int g = threadIdx.x - 64;
       const int c = g & 7;
@@ -290,19 +316,22 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
       const T* x = static_cast<const T*>(p.a_rows);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (int it = 0; ok; ++it) {
-        const int tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, it, &s_abort, p.err,
-                                             true);
-        if (tile < 0) break;
-        const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, tile, C::kOutCols);
-        const T* src[16];
+      int tok[16];
+      auto load_rows = [&](int t) {
+        const TileInfo ti = decode_tile(s_tp, s_off, E, p.n_tiles, t, C::kOutCols);
         const int last = ti.valid - 1;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int tok = __ldg(p.sorted_token + ti.row_base + min(q + 8 * i, last));
-          src[i] = x + static_cast<size_t>(tok) * p.K + c * 8;
-        }
+        for (int i = 0; i < 16; ++i)
+          tok[i] = __ldg(p.sorted_token + ti.row_base + min(q + 8 * i, last));
+      };
+      int tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, 0, &s_abort, p.err, true);
+      if (tile >= 0) load_rows(tile);
+      for (int it = 0; ok && tile >= 0; ++it) {
+        const T* src[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) src[i] = x + static_cast<size_t>(tok[i]) * p.K + c * 8;
         const uint32_t dst_off = static_cast<uint32_t>(q * 128 + ((c ^ q) << 4));
+        int next = -1;
         for (int kb = 0; kb < num_kb; ++kb) {
           bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
                                        kErrWaitEmpty);
@@ -319,7 +348,17 @@ __global__ void __launch_bounds__(kSm100Threads, 1)
             stage = 0;
             phase ^= 1u;
           }
+          if (kb == (num_kb - 1) / 2) {
+            next = peek_tile_in_ring(bar_tfull, s_tile, it + 1, &s_abort, p.err);
+            if (next == -2) {
+              ok = false;
+              break;
+            }
+            if (next >= 0) load_rows(next);
+          }
         }
+        if (!ok) break;
+        tile = next_tile_from_ring(bar_tfull, bar_tempty, s_tile, it + 1, &s_abort, p.err, true);
       }
     }
   } else {

@@ -1,7 +1,7 @@
 // The Qwen3 expert GEMMs on CTA pairs: tcgen05.mma.cta_group::2 with M = 256, so each SM stages
 // only half of the B tile.  GEMM-2 (y = h.D_e x routing weight, D_e [I,H] MN-major) is the
 // default path for fused calls; GEMM-1 (gate|up with the activation epilogue, gathered rows) is
-// opt-in (GEMM path 4): it is correct but measured 1.9x slower than the one-CTA GEMM-1 at config 5.
+// opt-in (GEMM path 4): correct, and as fast as the one-CTA GEMM-1 at configs 4 and 5, not faster.
 // The description below is GEMM-2's; GEMM-1's kernel says what differs.
 //
 // A cluster of two CTAs owns a pair tile: 256 sorted rows of one expert (each CTA 128 of them)
@@ -39,6 +39,13 @@ constexpr int kPAStage = kPBM * kPBK * 2;        // 16 KB
 constexpr int kPBStage = (kPBN / 2) * kPBK * 2;  // 16 KB: this CTA's half of the B columns
 constexpr int kPStageBytes = kPAStage + kPBStage;
 constexpr int kPThreads = 256;
+// GEMM-1: relay threads of the odd CTA (warp 1 and warps 8..), each taking every kP1Relays-th
+// stage, so that one relay's wait for its stage does not delay the next stage's relay.
+#ifndef CMOE_P1_RELAYS
+#define CMOE_P1_RELAYS 4
+#endif
+constexpr int kP1Relays = CMOE_P1_RELAYS;
+constexpr int kP1Threads = kPThreads + 32 * (kP1Relays - 1);
 constexpr int kPStageOut = 4 * 4096;
 constexpr size_t kPSmemBase = static_cast<size_t>(kPStages) * kPStageBytes + 1024 + kPStageOut;
 constexpr size_t kPSmemMax = 232448 - 1024;
@@ -58,9 +65,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
                ::: "memory");
 }
+// Arrival on a barrier of the other CTA of the pair, with the instruction's default semantics
+// (release at CTA scope), as CUTLASS's 2-SM pipelines arrive on the leader CTA's barriers.  An
+// explicit .release.cluster made each arrival wait 0.5-2.7 us for the SM's outstanding memory
+// traffic (measured with %globaltimer stamps in GEMM-1's relay at config 5).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -378,16 +388,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (warp == 2) tmem_dealloc_pair(tmem_base, 512);
 }
 
+// Relay `r` of the odd CTA (see sm100_gemm1_pair_kernel): for every kP1Relays-th stage, from
+// the r-th on, wait for this CTA's gather threads, then fence and arrive on the even CTA's full
+// barrier of that stage.
+__device__ __forceinline__ void pair_gemm1_relay(uint64_t* bar_full, int r, int pair, int pairs,
+                                                 int total_tiles, int num_kb, int* s_abort,
+                                                 uint32_t* err) {
+  uint32_t stage = 0, phase = 0;
+  int n = 0;
+  for (int tile = pair; tile < total_tiles; tile += pairs) {
+    for (int kb = 0; kb < num_kb; ++kb, ++n) {
+      if (n % kP1Relays == r) {
+        const uint32_t full_local = smem_addr(&bar_full[stage]);
+        if (!mbar_wait_bounded(full_local, phase, s_abort, err, kErrWaitFull)) return;
+        fence_proxy_async_smem();  // the gathered rows before the even CTA's MMA reads them
+        mbar_arrive_remote(mapa_shared(full_local, 0));
+      }
+      if (++stage == kPStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+}
+
 // GEMM-1 of the Qwen3 FFN on CTA pairs: h = act(x.G_e) * (x.U_e) for 256 gathered rows of one
 // expert and 128 intermediate columns.  Each CTA gathers its own 128 token rows with cp.async into
 // the swizzled A layout (warps 2-3) and stages one half of the N = 256 B tile: the even CTA the
 // gate columns, the odd CTA the up columns; both CTAs' TMEM then hold gate (columns 0-127) and
 // up (128-255) of their own rows.  The even CTA's full barrier counts its producer (expected B
-// bytes of both CTAs), its 64 gather threads and one relay arrival: the odd CTA's warp 1 waits
-// for its own gather threads on its local full barrier, orders their generic-proxy writes before
-// the tensor core's async-proxy reads (fence.proxy.async) and arrives remotely.
+// bytes of both CTAs), its 64 gather threads and one relay arrival: a relay thread of the odd CTA
+// waits for its own gather threads on its local full barrier, orders their generic-proxy writes
+// before the tensor core's async-proxy reads (fence.proxy.async) and arrives remotely.  The
+// stages are dealt round-robin to kP1Relays relay threads in separate warps (warp 1 and warps
+// 8..), so that the fences and remote arrivals of consecutive stages overlap.
 template <typename T>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kP1Threads, 1)
     sm100_gemm1_pair_kernel(const __grid_constant__ CUtensorMap tmG,
                             const __grid_constant__ CUtensorMap tmU, const Sm100Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -528,25 +564,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         umma_commit_pair(mapa_shared(accf_local, 1));
       }
     } else if (lane == 0 && rank == 1) {
-      // ---------------------------------------------------------------- relay (odd CTA)
-      uint32_t stage = 0, phase = 0;
-      bool ok = true;
-      for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
-        for (int kb = 0; kb < num_kb; ++kb) {
-          const uint32_t full_local = smem_addr(&bar_full[stage]);
-          if (!mbar_wait_bounded(full_local, phase, &s_abort, p.err, kErrWaitFull)) {
-            ok = false;
-            break;
-          }
-          fence_proxy_async_smem();  // the gathered rows before the even CTA's MMA reads them
-          mbar_arrive_remote(mapa_shared(full_local, 0));
-          if (++stage == kPStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
+      pair_gemm1_relay(bar_full, 0, pair, pairs, total_tiles, num_kb, &s_abort, p.err);
     }
+  } else if (warp >= 8) {
+    if (lane == 0 && rank == 1)
+      pair_gemm1_relay(bar_full, warp - 7, pair, pairs, total_tiles, num_kb, &s_abort, p.err);
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------------ A-row gather
     const int g = threadIdx.x - 64;
@@ -555,22 +577,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const T* x = static_cast<const T*>(p.a_rows);
     uint32_t stage = 0, phase = 0;
     bool ok = true;
-    for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
-      const int mt = tile / p.n_tiles;
+    // the row indices of this CTA's 128 rows of a tile, loaded while the previous tile streams
+    int tok[16];
+    auto load_rows = [&](int t) {
+      const int mt = t / p.n_tiles;
       const int e = expert_of_tile_smem(s_tp, E, mt);
       const int pm0 = (mt - s_tp[e]) * 2 * kPBM;
       const int row_base = s_off[e] + pm0 + static_cast<int>(rank) * kPBM;
       const int valid = min(kPBM, s_off[e + 1] - s_off[e] - pm0 - static_cast<int>(rank) * kPBM);
-      const T* src[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         // rows past the expert's last one repeat a valid row (their outputs are not written)
         const int sr = valid > 0 ? row_base + min(q + 8 * i, valid - 1) : s_off[e] + pm0;
-        const int tok = __ldg(p.sorted_token + sr);
-        src[i] = x + static_cast<size_t>(tok) * p.K + c * 8;
+        tok[i] = __ldg(p.sorted_token + sr);
       }
+    };
+    if (pair < total_tiles) load_rows(pair);
+    for (int tile = pair; ok && tile < total_tiles; tile += pairs) {
+      const T* src[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) src[i] = x + static_cast<size_t>(tok[i]) * p.K + c * 8;
       const uint32_t dst_off = static_cast<uint32_t>(q * 128 + ((c ^ q) << 4));
       for (int kb = 0; kb < num_kb; ++kb) {
+        if (kb == (num_kb - 1) / 2 && tile + pairs < total_tiles) load_rows(tile + pairs);
         bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
                                      kErrWaitEmpty);
         got = __all_sync(0xffffffffu, got);
@@ -588,7 +617,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
       }
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp - 4;
     const int r = q * 32 + lane;
@@ -722,7 +751,7 @@ int launch_sm100_gemm1_pair(int dtype, const CUtensorMap& g, const CUtensorMap& 
   if (p.N % (kPBN / 2) != 0 || p.K % kPBK != 0) return 1;
   const size_t smem = sm100_pair_smem_bytes(p.E);
   if (smem > kPSmemMax) return 2;
-  const dim3 grid(2 * pairs), block(kPThreads);
+  const dim3 grid(2 * pairs), block(kP1Threads);
   if (dtype == kBF16)
     sm100_gemm1_pair_kernel<__nv_bfloat16><<<grid, block, smem, s>>>(g, u, p);
   else if (dtype == kF16)
