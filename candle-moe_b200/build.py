@@ -24,7 +24,7 @@ COMMON = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibi
                  "-I", os.path.join(ROOT, "include"), "-I", CSRC]
 EXTRA = {"router.cu": ["--use_fast_math"], "router_proj.cu": ["--use_fast_math"]}
 SOURCES = ["router.cu", "router_proj.cu", "route_prep.cu", "moe_simt.cu", "moe_sm100.cu", "moe_sm100_pair.cu",
-           "moe_decode.cu", "ep_kernels.cu", "peer.cu", "capi.cu"]
+           "moe_decode.cu", "moe_tf32.cu", "ep_kernels.cu", "peer.cu", "capi.cu"]
 
 
 def _newest_header() -> float:

@@ -100,7 +100,7 @@ int init_device(int dev, DeviceState** out) {
     if (cudaMemset(d.err_word, 0, sizeof(uint32_t)) != cudaSuccess) return MOE_ERR_CUDA;
     const bool attrs_ok = route_prep_set_attributes() && sm100_set_attributes() &&
                           sm100_pair_set_attributes() && decode_set_attributes() &&
-                          router_project_set_attributes();
+                          router_project_set_attributes() && tf32x3_set_attributes();
     cudaGetLastError();  // attribute failures are reported here, not by a later call
     if (!attrs_ok) return MOE_ERR_CUDA;
     d.max_pairs = sm100_pair_max_clusters();
@@ -127,17 +127,21 @@ int current_device_state(DeviceState** out) {
 inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // 2-D tensor map over a row-major [outer, inner] matrix of 16-bit elements, 128-byte swizzle.
+// swizzle: the 128-byte swizzle with 16-byte granules, or (MN-major f32 operands of the TF32
+// MMA) with 32-byte granules.
 bool make_map_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, uint64_t outer,
-                 uint32_t box_inner, uint32_t box_outer) {
+                 uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   if (!g_encode) return false;
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint64_t strides[1] = {inner * (dtype == kF32 ? 4 : 2)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt =
-      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = dtype == kF32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -234,6 +238,17 @@ bool sm100_shape_ok(int dtype, const void* x, const void* g, const void* u, cons
   return true;
 }
 
+// f32 operands on the tensor cores (moe_tf32.cu): the same tile constraints as f16/bf16.
+bool tf32_shape_ok(int dtype, const void* x, const void* g, const void* u, const void* d,
+                   const void* out, int H, int I, int E, int moe_type) {
+  if (dtype != kF32) return false;
+  if (E > sm100_max_experts()) return false;
+  if (H % 128 != 0 || I % 128 != 0) return false;
+  if (!aligned16(x) || !aligned16(g) || !aligned16(u) || !aligned16(out)) return false;
+  if (moe_type == 0 && !aligned16(d)) return false;
+  return true;
+}
+
 // out_row == nullptr: the drop-in semantics (output [T,H], the k slots of a token combined).
 // out_row != nullptr: no combine; the weighted contribution of every routed (t, j) is written to
 // row out_row[t*k + j] of `output` (rows must be distinct).
@@ -258,15 +273,18 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   bool use_sm100 = sm100_shape_ok(static_cast<int>(dtype), input, gate, up, down, output, H, I,
                                   E, static_cast<int>(moe_type)) &&
                    ds->cc_major == 10 && g_encode != nullptr;
-  if (gpath == 1) use_sm100 = false;
-  if (gpath == 2 && !use_sm100) return MOE_ERR_UNSUPPORTED;
+  bool use_tf32 = tf32_shape_ok(static_cast<int>(dtype), input, gate, up, down, output, H, I, E,
+                                static_cast<int>(moe_type)) &&
+                  ds->cc_major == 10 && g_encode != nullptr;
+  if (gpath == 1) use_sm100 = use_tf32 = false;
+  if (gpath == 2 && !use_sm100 && !use_tf32) return MOE_ERR_UNSUPPORTED;
 
   const bool scatter = out_row != nullptr;
   // decode-sized calls: weight-streaming tensor-core kernels with the combine fused
   const int dec_n = (use_sm100 && !scatter)
                         ? decode_rows(T, H, I, E, static_cast<int>(dtype), gpath)
                         : 0;
-  const int bm = dec_n ? dec_n : use_sm100 ? sm100_tile_m() : simt_tile_m();
+  const int bm = dec_n ? dec_n : (use_sm100 || use_tf32) ? sm100_tile_m() : simt_tile_m();
   // scatter writes each contribution to its own output row: no slot buffer, no combine
   FusedLayout L = fused_layout(T, H, I, E, k, static_cast<int>(dtype), dec_n);
   if (scatter) L.total = L.slot;
@@ -494,6 +512,57 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
                               stream))
           ok = false;
       }
+    }
+    if (!ok) st = MOE_ERR_CUDA;
+    t_last_path = 2;
+  } else if (st == MOE_OK && use_tf32) {
+    // ---------------------------------------------------------------- f32: 3xTF32 GEMMs
+    const int mode1 = moe_type == 0 ? kModeG1Dual : kModeG1Single;
+    const int mode2 = moe_type == 0 ? kModeG2MN : kModeG2K;
+    const int bn1 = tf32x3_out_cols(mode1, I), bn2 = tf32x3_out_cols(mode2, H);
+    const int sms = gemm_sms(ds);
+    const CUtensorMapSwizzle mn32 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    CUtensorMap mA, mB0, mB1;
+    Sm100Params p;
+    p.a_rows = input;
+    p.offsets = offsets;
+    p.tile_prefix = tile_prefix;
+    p.sorted_token = s_token;
+    p.sorted_flat = s_flat;
+    p.sorted_w = s_w;
+    p.out_row = nullptr;
+    p.E = E;
+    p.act = act;
+    p.err = ds->err_word;
+    p.tile_counter = nullptr;
+    // GEMM-1 gathers its A rows with cp.async; mA (the intermediate) serves GEMM-2
+    bool ok = make_map_2d(&mA, dtype, inter, I, static_cast<uint64_t>(rows), 32, 128) &&
+              make_map_2d(&mB0, dtype, gate, I, static_cast<uint64_t>(E) * H, 32, 32, mn32) &&
+              make_map_2d(&mB1, dtype, up, I, static_cast<uint64_t>(E) * H, 32, 32, mn32);
+    if (ok) {
+      p.out = inter;
+      p.N = I;
+      p.K = H;
+      p.n_tiles = I / bn1;
+      const int64_t tiles = mtile_bound * p.n_tiles;
+      ok = launch_tf32x3_gemm(mode1, bn1, mA, mB0, mB1, p,
+                              static_cast<int>(tiles < sms ? tiles : sms), stream) == 0;
+    }
+    if (ev) cudaEventRecord(ev[2], stream);
+    if (ok) {
+      ok = mode2 == kModeG2MN
+               ? make_map_2d(&mB0, dtype, down, H, static_cast<uint64_t>(E) * I, 32, 32, mn32)
+               : make_map_2d(&mB0, dtype, up, I, static_cast<uint64_t>(E) * H, 32, bn2);
+    }
+    if (ok) {
+      p.out = slot;
+      p.out_row = out_row;
+      p.N = H;
+      p.K = I;
+      p.n_tiles = H / bn2;
+      const int64_t tiles = mtile_bound * p.n_tiles;
+      ok = launch_tf32x3_gemm(mode2, bn2, mA, mB0, mB0, p,
+                              static_cast<int>(tiles < sms ? tiles : sms), stream) == 0;
     }
     if (!ok) st = MOE_ERR_CUDA;
     t_last_path = 2;

@@ -99,6 +99,13 @@ int sm100_out_cols(int mode, int bn);
 int launch_sm100_gemm(int dtype, int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
 
+// ---- moe_tf32.cu (G1/G2 for f32 operands: three TF32 products on the tensor cores) ----------
+bool tf32x3_set_attributes();
+// Output columns of one tile of `mode` when the GEMM has N output columns.
+int tf32x3_out_cols(int mode, int N);
+int launch_tf32x3_gemm(int mode, int bn, const CUtensorMap& a, const CUtensorMap& b0,
+                       const CUtensorMap& b1, const Sm100Params& p, int grid, cudaStream_t s);
+
 // ---- moe_decode.cu (D1: decode-sized calls, weights as the MMA's A operand, stream-K) -------
 struct DecodeParams {
   const void* b_src;            // GEMM-1: x [T, K]; GEMM-2: intermediate [rows, K]

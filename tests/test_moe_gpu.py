@@ -157,8 +157,35 @@ def test_baseline_shapes_sampled(name, dtype, moe_type, act, T, H, I, E, k, bias
 
 def test_c2_nomic_f32_full_shape_all_tokens():
     """BASELINE config 2 at its own shape (f32 Nomic, 512 tokens, H768, I3072, 8 experts top-2,
-    GELU), every output element against the oracle at the f32 tolerance 1e-4."""
+    GELU), every output element against the oracle at the f32 tolerance 1e-4: the tensor-core
+    path (three TF32 products) and the FFMA path."""
     case = moe_case(2, T=512, H=768, I=3072, E=8, k=2, moe_type=1, dtype="f32")
+    candle_moe.device_error_bits(0, clear=True)
     got, used = run_gpu(case, 8, 2, 1, 1, "f32")
+    assert used == 2
+    assert candle_moe.device_error_bits(0) == 0
+    check_vs_oracle(got, case, 1, 1, "f32", "c2-nomic-f32-T512 3xTF32", rtol=1e-4)
+    got, used = run_gpu(case, 8, 2, 1, 1, "f32", path=1)
     assert used == 1
-    check_vs_oracle(got, case, 1, 1, "f32", "c2-nomic-f32-T512", rtol=1e-4)
+    check_vs_oracle(got, case, 1, 1, "f32", "c2-nomic-f32-T512 FFMA", rtol=1e-4)
+
+
+@pytest.mark.parametrize("moe_type,act,T,H,I,E,k", [
+    (1, 1, 300, 256, 384, 8, 2),    # Nomic GELU, GEMM-2 K-major B in 64-column tiles
+    (0, 0, 300, 256, 384, 8, 2),    # Qwen3 SwiGLU: gate|up as one N = 128 MMA, GEMM-2 MN-major
+    (0, 2, 77, 2048, 256, 16, 1),   # k = 1 (GEMM-2 writes the output), 128-column GEMM-2 tiles
+    (1, 0, 1000, 128, 128, 4, 4),   # one 128-wide GEMM-1 tile per m-tile, many m-tiles
+])
+def test_f32_tensor_core_path_vs_oracle(moe_type, act, T, H, I, E, k):
+    """f32 on the tensor cores (moe_tf32.cu) against the oracle at 1e-4 relative, and against
+    the FFMA path on the same inputs."""
+    case = moe_case(91 + T + act, T=T, H=H, I=I, E=E, k=k, moe_type=moe_type, dtype="f32",
+                    renormalize=(moe_type == 0))
+    candle_moe.device_error_bits(0, clear=True)
+    got, used = run_gpu(case, E, k, act, moe_type, "f32")
+    assert used == 2
+    assert candle_moe.device_error_bits(0) == 0
+    check_vs_oracle(got, case, act, moe_type, "f32", f"3xTF32 {moe_type} {act}", rtol=1e-4)
+    simt, used = run_gpu(case, E, k, act, moe_type, "f32", path=1)
+    assert used == 1
+    check_close(got, simt, 1e-4, "3xTF32 vs FFMA")

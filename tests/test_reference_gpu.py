@@ -75,6 +75,8 @@ REF_MOE = [
     ("f32", 1, 0, 512, 64, 256, 8, 2),     # f32 FFMA
     ("f32", 0, 0, 300, 96, 160, 8, 2),     # f32 FFMA
     ("f32", 1, 1, 100, 32, 128, 8, 2),     # f32 FFMA, GELU
+    ("f32", 1, 1, 256, 256, 384, 8, 2),    # f32 FFMA here; ours on the tensor cores (3xTF32)
+    ("f32", 0, 0, 200, 128, 256, 8, 2),    # same, Qwen3 SwiGLU
     ("bf16", 0, 0, 8, 256, 512, 8, 2),     # direct (T <= 32)
     ("f16", 1, 2, 32, 128, 256, 8, 2),     # direct, ReLU
     ("f16", 0, 0, 48, 64, 256, 8, 1),      # small wmma GEMM (k=1, 33 <= T <= 64)
