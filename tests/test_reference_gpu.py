@@ -32,6 +32,23 @@ def test_router_bit_exact_vs_reference(E, k):
     assert torch.equal(w.view(torch.int32), rw.view(torch.int32))  # bit-identical weights
 
 
+@pytest.mark.parametrize("E", [128, 256])
+@pytest.mark.parametrize("k", [3, 16, 32, 33])
+@pytest.mark.parametrize("T", [1, 77, 4096])
+def test_router_large_expert_counts_many_k_bit_exact_vs_reference(E, k, T):
+    """128 and 256 experts (a warp per row), odd and large k, a single token and ragged counts,
+    rows with ties: bit-identical to the reference kernel."""
+    x = oracle.randn(E * k + T, (T, E))
+    x[::5] = np.round(x[::5])  # rows with ties
+    x = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    rw, ri, rs = refkernels.topk_softmax(x, k)
+    w, i, s = candle_moe.topk_softmax(x, k)
+    torch.cuda.synchronize()
+    assert torch.equal(i, ri)
+    assert torch.equal(s, rs)
+    assert torch.equal(w.view(torch.int32), rw.view(torch.int32))
+
+
 @pytest.mark.parametrize("E", [8, 128, 256])
 def test_router_ties_and_non_finite_rows_bit_exact_vs_reference(E):
     """Logits from a 5-value set (ties on every row), plus rows with -inf, +inf and NaN logits:
