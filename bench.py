@@ -389,7 +389,16 @@ def run_ours(args, world, rank, local):
         # flops[] are per step; with expert parallelism a step makes several fused calls
         tflops = {p: flops[p] / (per_step[p] / 1e3) / 1e12 for p in ("gemm1", "gemm2")}
         step_tflops = (flops["gemm1"] + flops["gemm2"]) / (ms_step / 1e3) / 1e12
-        if dtype == "f32":
+        if dtype == "f32" and candle_moe.last_gemm_path() == 2:
+            # f32 on the tensor cores: three TF32 products per f32 product, and TF32 runs at
+            # half the f16/bf16 dense rate, so the f32-equivalent peak is the measured bf16
+            # burst / 6 (no TF32 peak is measured on this pool)
+            peak = peaks.get("bf16_tflops") / 6.0
+            peak_sus = peaks.get("bf16_tflops_sustained") / 6.0
+            kernel, bound = "tf32x3_grouped_gemm", "tensor"
+            kind = (f"{peak_kind} bf16 dense burst / 2 (TF32 rate) / 3 (products per f32 "
+                    f"product); MEASURED_PEAKS.json")
+        elif dtype == "f32":
             # the f32 path runs on the FP32 pipes (SIMT kernel); no measured FP32 peak exists
             # on this pool, so the nominal one: 148 SMs x 128 lanes x 2 FLOP x 1965 MHz
             peak = 148 * 128 * 2 * 1.965e9 / 1e12

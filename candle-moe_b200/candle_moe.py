@@ -93,8 +93,6 @@ def lib() -> ctypes.CDLL:
         L.moe_combine_rows.restype = ctypes.c_int
         L.moe_set_sm_reserve.argtypes = [I32]
         L.moe_set_sm_reserve.restype = I32
-        L.moe_set_decode_fused.argtypes = [I32]
-        L.moe_set_decode_fused.restype = I32
         L.moe_kernel_launches.argtypes = []
         L.moe_kernel_launches.restype = I64
         L.moe_phase_timing.argtypes = [I32]
@@ -630,12 +628,6 @@ class SparseMoeBlock:
 
 def device_error_bits(device: int = 0, clear: bool = False) -> int:
     return int(lib().moe_device_error_bits(device, int(clear)))
-
-
-def set_decode_fused(enable: bool) -> bool:
-    """Decode calls: both GEMMs in one cooperative kernel (True, the default) or two kernels;
-    returns the previous setting."""
-    return bool(lib().moe_set_decode_fused(1 if enable else 0))
 
 
 def set_gemm_path(path: int) -> int:

@@ -30,8 +30,6 @@ thread_local int t_last_status = MOE_OK;
 thread_local int t_last_path = 0;
 std::atomic<int> g_gemm_path{0};
 std::atomic<int> g_sm_reserve{0};  // SMs the persistent GEMMs leave free (moe_set_sm_reserve)
-// decode calls: both GEMMs in one cooperative kernel (1) or two kernels (0); moe_set_decode_fused
-std::atomic<int> g_decode_one{1};
 
 constexpr int kMaxDevices = 64;
 
@@ -169,7 +167,6 @@ struct FusedLayout {
   size_t offsets, tile_prefix, counters, sorted_token, sorted_flat, sorted_w, prep_scratch, inter,
       slot, dec_part, dec_cnt, total;
   int64_t dec_units1, dec_units2;  // unit-counter capacity of the decode GEMMs
-  int64_t dec_chunks;              // chunk-counter capacity (single-kernel decode)
 };
 
 // dec_n: rows per chunk of the decode kernels (0: the grouped GEMMs run).
@@ -189,19 +186,16 @@ FusedLayout fused_layout(int64_t T, int H, int I, int E, int k, int dtype, int d
   // the decode kernels always combine through the (token, slot) rows, also for k = 1
   L.slot = o;           o += (k > 1 || dec_n) ? align256(elt * static_cast<size_t>(rows) * H) : 0;
   L.dec_part = o;
-  L.dec_units1 = L.dec_units2 = L.dec_chunks = 0;
+  L.dec_units1 = L.dec_units2 = 0;
   if (dec_n) {
     // one region per GEMM: GEMM-2 starts while GEMM-1's last units are being finished
     o += 2 * align256(decode_partial_bytes(dec_n, decode_max_grid()));
     const int64_t chunks = rows / dec_n + (E < rows ? E : rows);
     L.dec_units1 = chunks * (I / 128);
     L.dec_units2 = chunks * (H / 128);
-    L.dec_chunks = chunks;
   }
   L.dec_cnt = o;
-  if (dec_n)
-    o += align256(sizeof(uint32_t) *
-                  (4 * (L.dec_units1 + L.dec_units2 + H / 128) + L.dec_chunks));
+  if (dec_n) o += align256(sizeof(uint32_t) * 4 * (L.dec_units1 + L.dec_units2 + H / 128));
   L.total = o;
   return L;
 }
@@ -321,8 +315,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   if (dec_n) {
     // the decode kernels' counters, zeroed before the route preparation so that GEMM-1 follows
     // it directly (it is launched as the route preparation's programmatic dependent)
-    const size_t ncnt =
-        4 * static_cast<size_t>(L.dec_units1 + L.dec_units2 + H / 128) + L.dec_chunks;
+    const size_t ncnt = 4 * static_cast<size_t>(L.dec_units1 + L.dec_units2 + H / 128);
     if (cudaMemsetAsync(ws + L.dec_cnt, 0, ncnt * sizeof(uint32_t), stream) != cudaSuccess)
       st = MOE_ERR_CUDA;
   }
@@ -363,40 +356,7 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
               (mode2 == kModeG2MN
                    ? make_map_2d(&mW2, dtype, down, H, static_cast<uint64_t>(E) * I, 64, 64)
                    : make_map_2d(&mW2, dtype, up, I, static_cast<uint64_t>(E) * H, 64, 128));
-    bool one = false;
-    if (ok && g_decode_one.load()) {
-      // both GEMMs in one cooperative kernel; if the launch is refused, the two kernels below
-      DecodeOneParams q;
-      q.x = input;
-      q.inter = inter;
-      q.slot = ws + L.slot;
-      q.out = output;
-      q.offsets = offsets;
-      q.chunk_prefix = tile_prefix;
-      q.sorted_token = s_token;
-      q.sorted_flat = s_flat;
-      q.sorted_w = s_w;
-      q.idx = idx;
-      q.partials1 = reinterpret_cast<float*>(ws + L.dec_part);
-      q.partials2 = reinterpret_cast<float*>(
-          ws + L.dec_part + align256(decode_partial_bytes(dec_n, decode_max_grid())));
-      q.unit_counter1 = dcnt;
-      q.unit_counter2 = dcnt + 4 * L.dec_units1;
-      q.tile_counter = dcnt + 4 * (L.dec_units1 + L.dec_units2);
-      q.chunk_done = dcnt + 4 * (L.dec_units1 + L.dec_units2 + H / 128);
-      q.err = ds->err_word;
-      q.H = H;
-      q.I = I;
-      q.E = E;
-      q.act = act;
-      q.k = k;
-      q.num_tokens = static_cast<int>(T);
-      one = launch_decode_one(static_cast<int>(dtype), static_cast<int>(moe_type), dec_n, mA0,
-                              mA1, mW2, q, grid, stream) == 0;
-    }
-    if (ok && one) {
-      if (ev) cudaEventRecord(ev[2], stream);
-    } else if (ok) {
+    if (ok) {
       p.b_src = input;
       p.out = inter;
       p.final_out = nullptr;
@@ -405,9 +365,9 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       p.M = I;
       p.K = H;
       ok = launch_decode_ffn(static_cast<int>(dtype), mode1, dec_n, mA0, mA1, p, grid, stream) == 0;
-      if (ev) cudaEventRecord(ev[2], stream);
     }
-    if (ok && !one) {
+    if (ev) cudaEventRecord(ev[2], stream);
+    if (ok) {
       p.b_src = inter;
       p.out = ws + L.slot;
       p.final_out = output;
@@ -421,7 +381,6 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
     }
     if (!ok && st == MOE_OK) st = MOE_ERR_CUDA;
     if (ev) cudaEventRecord(ev[3], stream);
-    if (one) --launches;  // one kernel where the count below assumes two
     t_last_path = 3;
   } else if (st == MOE_OK && use_sm100) {
     if (cudaMemsetAsync(counters, 0, 2 * sizeof(uint32_t), stream) != cudaSuccess) st = MOE_ERR_CUDA;
@@ -977,11 +936,6 @@ CMOE_API int32_t moe_last_gemm_path(void) { return t_last_path; }
 CMOE_API int32_t moe_set_sm_reserve(int32_t sms) {
   if (sms < 0 || sms > 128) return -1;
   return g_sm_reserve.exchange(sms);
-}
-
-CMOE_API int32_t moe_set_decode_fused(int32_t enable) {
-  if (enable != 0 && enable != 1) return -1;
-  return g_decode_one.exchange(enable);
 }
 
 CMOE_API int64_t moe_kernel_launches(void) { return g_launches.load(); }

@@ -133,30 +133,6 @@ size_t decode_partial_bytes(int n, int grid);
 bool decode_set_attributes();
 int launch_decode_ffn(int dtype, int mode, int n, const CUtensorMap& a0, const CUtensorMap& a1,
                       const DecodeParams& p, int grid, cudaStream_t s);
-// Both decode GEMMs in one cooperative kernel (GEMM-2 waits per chunk for GEMM-1's rows).
-struct DecodeOneParams {
-  const void* x;                 // [T, H]
-  void* inter;                   // [rows, I] intermediate, expert-sorted rows
-  void* slot;                    // [T*k, H] (token, slot) rows
-  void* out;                     // [T, H]
-  const int32_t* offsets;        // [E+2]
-  const int32_t* chunk_prefix;   // [E+1], tile height N
-  const int32_t* sorted_token;
-  const int32_t* sorted_flat;
-  const float* sorted_w;
-  const uint32_t* idx;           // [T*k]
-  float* partials1;              // GEMM-1 stream-K partials
-  float* partials2;              // GEMM-2 stream-K partials
-  uint32_t* unit_counter1;       // [4 * units1]
-  uint32_t* unit_counter2;       // [4 * units2]
-  uint32_t* tile_counter;        // [4 * H/128]
-  uint32_t* chunk_done;          // [chunks]: GEMM-1 (unit, quarter) finishes per chunk
-  uint32_t* err;
-  int H, I, E, act, k, num_tokens;
-};
-
-int launch_decode_one(int dtype, int moe_type, int n, const CUtensorMap& g, const CUtensorMap& u,
-                      const CUtensorMap& w2, const DecodeOneParams& p, int grid, cudaStream_t s);
 
 // ---- ep_kernels.cu -------------------------------------------------------------------------
 constexpr int kMaxEpBins = 12288;  // (chunk, rank) counters of ep_dest_groups (48 KB smem)

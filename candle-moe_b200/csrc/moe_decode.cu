@@ -543,482 +543,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 }
 
-// ---- both GEMMs in one kernel ----------------------------------------------------------------
-//
-// The two kernels above pay a kernel boundary between GEMM-1 and GEMM-2: GEMM-1's last stream-K
-// exchanges (partial stores, counters, partial loads) end its stream several microseconds before
-// it completes, and GEMM-2 starts streaming only a ring's worth of weights before it must wait
-// for all of GEMM-1.  decode_ffn_one_kernel runs GEMM-1's pieces and then GEMM-2's pieces in
-// every CTA, through one operand ring and one pair of TMEM accumulator buffers: as soon as a
-// CTA has issued its last GEMM-1 tile its producer streams its GEMM-2 weight tiles, and GEMM-2's
-// row gather waits per chunk -- not for the whole of GEMM-1 -- until the chunk's intermediate
-// rows are final (a counter per chunk, raised with release semantics by every warp that
-// finishes a GEMM-1 unit of the chunk, read with acquire semantics; bounded wait).  That wait is
-// on other CTAs' progress, so the kernel is launched cooperatively (all CTAs resident); GEMM-1
-// work never waits on GEMM-2 work (it comes first in every CTA's ring), so the waits end.
-
-// Acquire load of a counter another CTA raises (gpu scope).
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Work of one CTA over both phases: GEMM-1's pieces, then GEMM-2's.
-struct DecWork2 {
-  DecWork w[2];
-  int phase;
-};
-__device__ __forceinline__ bool dec_next2(DecWork2& d, const int (&KB)[2], int& ph, int64_t& u,
-                                          int& kb_lo, int& kb_hi) {
-  while (d.phase < 2) {
-    if (dec_next(d.w[d.phase], KB[d.phase], u, kb_lo, kb_hi)) {
-      ph = d.phase;
-      return true;
-    }
-    ++d.phase;
-  }
-  return false;
-}
-
-template <int MODE1, int MODE2, int N>
-struct DecOneCfg {
-  using C1 = DecCfg<MODE1, N>;
-  using C2 = DecCfg<MODE2, N>;
-  static constexpr int kStageBytes =
-      C1::kStageBytes > C2::kStageBytes ? C1::kStageBytes : C2::kStageBytes;
-  static constexpr int kRing = 200 * 1024;
-  static constexpr int kStages = kRing / kStageBytes > 8 ? 8 : kRing / kStageBytes;
-  static constexpr int kAccCols = C1::kAccCols > C2::kAccCols ? C1::kAccCols : C2::kAccCols;
-  static constexpr int kTmemCols = 2 * kAccCols <= 32 ? 32 : 2 * kAccCols <= 64 ? 64
-                                 : 2 * kAccCols <= 128 ? 128 : 256;
-};
-
-// The epilogue of one piece of phase PH (0: GEMM-1, 1: GEMM-2): accumulator out of TMEM, the
-// stream-K exchange when the piece is cut, and the unit's finish.  Returns false when the
-// accumulator wait gave up.
-template <typename T, int PH, int MODE, int N>
-__device__ __forceinline__ bool dec_one_epilogue(
-    const DecodeOneParams& p, const int32_t* s_cp, const int32_t* s_off, int E, int MT, int KB,
-    int G, int64_t W, int64_t first_unit, int64_t u, int kb_lo, int kb_hi, int chunks,
-    uint32_t tmem_base, int acc_stride, int piece, uint64_t* bar_accf, uint64_t* bar_acce,
-    volatile int* s_abort, int q, int lane) {
-  using C = DecCfg<MODE, N>;
-  const int m = q * 32 + lane;
-  const DecUnit d = dec_unit(s_cp, s_off, E, MT, u);
-  const int chunk = static_cast<int>(u / MT);
-  const int base = s_off[d.e] + (chunk - s_cp[d.e]) * N;
-  const int valid = min(N, s_off[d.e + 1] - base);
-  const int buf = piece & 1;
-  bool got = mbar_wait_bounded(smem_addr(&bar_accf[buf]), static_cast<uint32_t>((piece >> 1) & 1),
-                               s_abort, p.err, kErrWaitAccFull);
-  got = __all_sync(0xffffffffu, got);
-  if (!got) return false;
-  tc_fence_after();
-  float v[C::kAccCols];
-  const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(buf * acc_stride);
-#pragma unroll
-  for (int c0 = 0; c0 < C::kAccCols; c0 += 16) {
-    uint32_t r[16];
-    tmem_ld_32x32b_x16(tb + c0, r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[c0 + i] = __uint_as_float(r[i]);
-  }
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(smem_addr(&bar_acce[buf]));
-
-  if (kb_lo != 0 || kb_hi != KB) {
-    float* part = PH == 0 ? p.partials1 : p.partials2;
-    uint32_t* ucnt = PH == 0 ? p.unit_counter1 : p.unit_counter2;
-    float* sp = part + (static_cast<size_t>(blockIdx.x) * 2 + (u == first_unit ? 0 : 1)) *
-                           C::kPartFloats;
-#pragma unroll
-    for (int i = 0; i < C::kAccCols; ++i) __stcg(sp + i * kDecM + m, v[i]);
-    __syncwarp();
-    const int64_t lo = u * KB, hi = lo + KB;
-    int64_t c_lo = lo * G / W;
-    while (c_lo > 0 && sk_start(c_lo, W, G) > lo) --c_lo;
-    while (sk_start(c_lo + 1, W, G) <= lo) ++c_lo;
-    uint32_t pieces = 0;
-    for (int64_t cc = c_lo; cc < G && sk_start(cc, W, G) < hi; ++cc)
-      if (sk_start(cc + 1, W, G) > sk_start(cc, W, G)) ++pieces;
-    uint32_t old = 0;
-    if (lane == 0) old = atom_add_acq_rel_gpu(ucnt + u * 4 + q, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 != pieces) return true;
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < C::kAccCols; ++i) v[i] = 0.f;
-    for (int64_t cc = c_lo; cc < G && sk_start(cc, W, G) < hi; ++cc) {
-      const int64_t s0 = sk_start(cc, W, G);
-      if (sk_start(cc + 1, W, G) <= s0) continue;
-      const float* pp =
-          part + (static_cast<size_t>(cc) * 2 + (u == s0 / KB ? 0 : 1)) * C::kPartFloats;
-#pragma unroll
-      for (int i = 0; i < C::kAccCols; ++i) v[i] += __ldcg(pp + i * kDecM + m);
-    }
-  }
-
-  const int col = d.mt * kDecM + m;
-  if (PH == 0) {
-    T* inter = static_cast<T*>(p.inter);
-#pragma unroll
-    for (int n = 0; n < N; ++n) {
-      if (n < valid) {
-        const float h = C::kDual ? act_apply(v[n], p.act) * v[N + n] : act_apply(v[n], p.act);
-        inter[static_cast<size_t>(base + n) * p.I + col] = Elem<T>::from_f(h);
-      }
-    }
-    // this warp's 32 columns of the chunk's rows are final
-    __syncwarp();
-    if (lane == 0) red_release_gpu_add(p.chunk_done + chunk, 1u);
-    return true;
-  }
-  T* slot = static_cast<T*>(p.slot);
-  constexpr int kR = N > 32 ? N / 32 : 1;
-  int fl[kR];
-  float wl[kR];
-#pragma unroll
-  for (int i = 0; i < kR; ++i) {
-    const int r = i * 32 + lane;
-    fl[i] = r < valid ? __ldg(p.sorted_flat + base + r) : 0;
-    wl[i] = r < valid ? __ldg(p.sorted_w + base + r) : 0.f;
-  }
-#pragma unroll
-  for (int n = 0; n < N; ++n) {
-    const int flat = __shfl_sync(0xffffffffu, fl[n / 32], n % 32);
-    const float wgt = __shfl_sync(0xffffffffu, wl[n / 32], n % 32);
-    if (n < valid) slot[static_cast<size_t>(flat) * p.H + col] = Elem<T>::from_f(v[n] * wgt);
-  }
-  __syncwarp();
-  uint32_t old = 0;
-  if (lane == 0) old = atom_add_acq_rel_gpu(p.tile_counter + d.mt * 4 + q, 1u);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old + 1 == static_cast<uint32_t>(chunks)) {
-    __syncwarp();
-    T* out = static_cast<T*>(p.out);
-    const int k = p.k;
-    const int T_ = p.num_tokens;
-    const int tb2 = k < 32 ? 32 / k : 1;
-    for (int t0 = 0; t0 < T_; t0 += tb2) {
-      const int nf = min(tb2, T_ - t0) * k;
-      const int f0 = t0 * k;
-      const bool ok_j = lane < nf && __ldg(p.idx + f0 + lane) < static_cast<uint32_t>(E);
-      const uint32_t okm = __ballot_sync(0xffffffffu, ok_j);
-      unsigned short raw[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int f = (okm >> j) & 1u ? f0 + j : f0;
-        raw[j] = __ldcg(reinterpret_cast<const unsigned short*>(slot) +
-                        static_cast<size_t>(f) * p.H + col);
-      }
-      float acc = 0.f;
-      int jj = 0;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (j < nf) {
-          if ((okm >> j) & 1u) acc += raw_to_f<T>(raw[j]);
-          if (++jj == k) {
-            out[static_cast<size_t>(t0 + j / k) * p.H + col] = Elem<T>::from_f(acc);
-            acc = 0.f;
-            jj = 0;
-          }
-        }
-      }
-    }
-  }
-  return true;
-}
-
-template <typename T, int MODE1, int MODE2, int N>
-__global__ void __launch_bounds__(kDecThreads, 1)
-    decode_ffn_one_kernel(const __grid_constant__ CUtensorMap tmG,
-                          const __grid_constant__ CUtensorMap tmU,
-                          const __grid_constant__ CUtensorMap tmW2, const DecodeOneParams p) {
-  using O = DecOneCfg<MODE1, MODE2, N>;
-  using C1 = typename O::C1;
-  using C2 = typename O::C2;
-  constexpr int kStages = O::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bar_full[kStages];
-  __shared__ __align__(8) uint64_t bar_empty[kStages];
-  __shared__ __align__(8) uint64_t bar_accf[2];
-  __shared__ __align__(8) uint64_t bar_acce[2];
-  __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
-
-  const uint32_t raw = smem_addr(smem_raw);
-  const uint32_t smem_base = (raw + 1023u) & ~1023u;
-  int32_t* s_cp = reinterpret_cast<int32_t*>(smem_raw + (smem_base - raw) +
-                                             static_cast<size_t>(kStages) * O::kStageBytes);
-  int32_t* s_off = s_cp + (p.E + 1);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int E = p.E;
-  const int G = static_cast<int>(gridDim.x);
-  const int MT[2] = {p.I / kDecM, p.H / kDecM};
-  const int KB[2] = {p.H / kDecK, p.I / kDecK};
-
-  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
-    s_cp[i] = __ldg(p.chunk_prefix + i);
-    s_off[i] = __ldg(p.offsets + i);
-  }
-  __syncthreads();
-  const int chunks = s_cp[E];
-  if (chunks == 0) {
-    // no routed row at all: the output is zeros
-    T* out = static_cast<T*>(p.out);
-    const int64_t n = static_cast<int64_t>(p.num_tokens) * p.H;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<int64_t>(G) * blockDim.x)
-      out[i] = Elem<T>::from_f(0.f);
-    return;
-  }
-  int64_t W[2];
-  DecWork2 work0;
-  work0.w[0] = dec_work(static_cast<int64_t>(chunks) * MT[0], KB[0], G,
-                        static_cast<int>(blockIdx.x), &W[0]);
-  work0.w[1] = dec_work(static_cast<int64_t>(chunks) * MT[1], KB[1], G,
-                        static_cast<int>(blockIdx.x), &W[1]);
-  work0.phase = 0;
-  const uint32_t chunk_target = static_cast<uint32_t>(MT[0]) * 4u;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_addr(&bar_full[s]), 1 + 64);
-      mbar_init(smem_addr(&bar_empty[s]), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_addr(&bar_accf[b]), 1);
-      mbar_init(smem_addr(&bar_acce[b]), 4);
-    }
-    s_abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmG);
-    if (C1::kDual) tma_prefetch_desc(&tmU);
-    tma_prefetch_desc(&tmW2);
-  }
-  if (warp == 2) {
-    tmem_alloc(smem_addr(&s_tmem), O::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = s_tmem;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (weights)
-    if (lane == 0) {
-      uint32_t stage = 0, phase = 0;
-      bool ok = true;
-      DecWork2 work = work0;
-      int ph;
-      int64_t u;
-      int kb_lo, kb_hi;
-      while (ok && dec_next2(work, KB, ph, u, kb_lo, kb_hi)) {
-        const DecUnit d = dec_unit(s_cp, s_off, E, MT[ph], u);
-        const int m0 = d.mt * kDecM;
-        for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
-                                 kErrWaitEmpty)) {
-            ok = false;
-            break;
-          }
-          const uint32_t full = smem_addr(&bar_full[stage]);
-          const uint32_t a_dst = smem_base + stage * O::kStageBytes;
-          if (ph == 0) {
-            mbar_arrive_expect_tx(full, C1::kABytes);
-            const int krow = d.e * p.H + kb * kDecK;
-            tma_load_2d(a_dst, &tmG, full, m0, krow);
-            tma_load_2d(a_dst + 8192, &tmG, full, m0 + 64, krow);
-            if (C1::kDual) {
-              tma_load_2d(a_dst + 16384, &tmU, full, m0, krow);
-              tma_load_2d(a_dst + 16384 + 8192, &tmU, full, m0 + 64, krow);
-            }
-          } else {
-            mbar_arrive_expect_tx(full, C2::kABytes);
-            if (C2::kAMN) {
-              const int krow = d.e * p.I + kb * kDecK;
-              tma_load_2d(a_dst, &tmW2, full, m0, krow);
-              tma_load_2d(a_dst + 8192, &tmW2, full, m0 + 64, krow);
-            } else {
-              tma_load_2d(a_dst, &tmW2, full, kb * kDecK, d.e * p.H + m0);
-            }
-          }
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc1 = dec_idesc(DecFmt<T>::v, 1u, N);
-      constexpr uint32_t idesc2 = dec_idesc(DecFmt<T>::v, C2::kAMN ? 1u : 0u, N);
-      uint32_t stage = 0, phase = 0;
-      bool ok = true;
-      int piece = 0;
-      DecWork2 work = work0;
-      int ph;
-      int64_t u;
-      int kb_lo, kb_hi;
-      for (; ok && dec_next2(work, KB, ph, u, kb_lo, kb_hi); ++piece) {
-        const int buf = piece & 1;
-        if (!mbar_wait_bounded(smem_addr(&bar_acce[buf]),
-                               static_cast<uint32_t>((piece >> 1) & 1) ^ 1u, &s_abort, p.err,
-                               kErrWaitAccEmpty)) {
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * O::kAccCols);
-        for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait_bounded(smem_addr(&bar_full[stage]), phase, &s_abort, p.err,
-                                 kErrWaitFull)) {
-            ok = false;
-            break;
-          }
-          fence_proxy_async_smem();
-          tc_fence_after();
-          const uint32_t a_base = smem_base + stage * O::kStageBytes;
-          const uint32_t b_base = a_base + (ph == 0 ? C1::kABytes : C2::kABytes);
-#pragma unroll
-          for (int ks = 0; ks < kDecK / 16; ++ks) {
-            const uint64_t bdesc = umma_sdesc(b_base + ks * 32, 16, 1024);
-            const uint32_t acc = (kb != kb_lo || ks != 0) ? 1u : 0u;
-            if (ph == 0) {
-              umma_f16(d, umma_sdesc(a_base + ks * 2048, 8192, 1024), bdesc, idesc1, acc);
-              if (C1::kDual)
-                umma_f16(d + N, umma_sdesc(a_base + 16384 + ks * 2048, 8192, 1024), bdesc,
-                         idesc1, acc);
-            } else if (C2::kAMN) {
-              umma_f16(d, umma_sdesc(a_base + ks * 2048, 8192, 1024), bdesc, idesc2, acc);
-            } else {
-              umma_f16(d, umma_sdesc(a_base + ks * 32, 16, 1024), bdesc, idesc2, acc);
-            }
-          }
-          umma_commit(smem_addr(&bar_empty[stage]));
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        umma_commit(smem_addr(&bar_accf[buf]));
-      }
-    }
-  } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------------ B-row gather
-    const int g = threadIdx.x - 64;
-    const int c = g & 7;
-    const int q = g >> 3;
-    uint32_t stage = 0, phase = 0;
-    bool ok = true;
-    DecWork2 work = work0;
-    int ph;
-    int64_t u;
-    int kb_lo, kb_hi;
-    while (ok && dec_next2(work, KB, ph, u, kb_lo, kb_hi)) {
-      const DecUnit d = dec_unit(s_cp, s_off, E, MT[ph], u);
-      const int chunk = static_cast<int>(u / MT[ph]);
-      const int base = s_off[d.e] + (chunk - s_cp[d.e]) * N;
-      const int last = min(N, s_off[d.e + 1] - base) - 1;
-      const int K = ph == 0 ? p.H : p.I;
-      const T* src_base = static_cast<const T*>(ph == 0 ? p.x : p.inter);
-      if (ph == 1) {
-        // GEMM-2 reads the chunk's intermediate rows: wait until every GEMM-1 unit of the chunk
-        // is finished (bounded; the waited-on work belongs to resident CTAs and waits on nothing)
-        bool ready = true;
-        if (lane == 0) {
-          const unsigned long long t0 = globaltimer_ns();
-          while (ld_acquire_gpu(p.chunk_done + chunk) < chunk_target) {
-            if (s_abort) {
-              ready = false;
-              break;
-            }
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-              s_abort = 1;
-              atomicOr(p.err, kErrWaitFull);
-              ready = false;
-              break;
-            }
-          }
-        }
-        ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
-        __syncwarp();
-        if (!ready) break;
-      }
-      const T* src[N / 8];
-#pragma unroll
-      for (int i = 0; i < N / 8; ++i) {
-        const int r = base + min(q + 8 * i, last);
-        const int row = ph == 0 ? __ldg(p.sorted_token + r) : r;
-        src[i] = src_base + static_cast<size_t>(row) * K + c * 8;
-      }
-      const uint32_t dst_off = static_cast<uint32_t>(q * 128 + ((c ^ q) << 4));
-      const int a_bytes = ph == 0 ? C1::kABytes : C2::kABytes;
-      for (int kb = kb_lo; kb < kb_hi; ++kb) {
-        bool got = mbar_wait_bounded(smem_addr(&bar_empty[stage]), phase ^ 1u, &s_abort, p.err,
-                                     kErrWaitEmpty);
-        got = __all_sync(0xffffffffu, got);
-        if (!got) {
-          ok = false;
-          break;
-        }
-        const uint32_t b_dst = smem_base + stage * O::kStageBytes + a_bytes + dst_off;
-#pragma unroll
-        for (int i = 0; i < N / 8; ++i) cp_async16(b_dst + i * 8 * 128, src[i] + kb * kDecK);
-        cp_async_mbar_arrive_noinc(smem_addr(&bar_full[stage]));
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------------------ epilogue (warps 4-7)
-    const int q = warp & 3;
-    int piece = 0;
-    DecWork2 work = work0;
-    int ph;
-    int64_t u;
-    int kb_lo, kb_hi;
-    for (; dec_next2(work, KB, ph, u, kb_lo, kb_hi); ++piece) {
-      const bool ok =
-          ph == 0 ? dec_one_epilogue<T, 0, MODE1, N>(p, s_cp, s_off, E, MT[0], KB[0], G, W[0],
-                                                     work0.w[0].w / KB[0], u, kb_lo, kb_hi,
-                                                     chunks, tmem_base, O::kAccCols, piece,
-                                                     bar_accf, bar_acce, &s_abort, q, lane)
-                  : dec_one_epilogue<T, 1, MODE2, N>(p, s_cp, s_off, E, MT[1], KB[1], G, W[1],
-                                                     work0.w[1].w / KB[1], u, kb_lo, kb_hi,
-                                                     chunks, tmem_base, O::kAccCols, piece,
-                                                     bar_accf, bar_acce, &s_abort, q, lane);
-      if (!ok) break;
-    }
-  }
-
-  __syncthreads();
-  if (s_abort) {
-    const unsigned long long t0 = globaltimer_ns();
-    while (globaltimer_ns() - t0 < 2000000ull) {
-    }
-  }
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, O::kTmemCols);
-  }
-}
-
 // ---- host side -------------------------------------------------------------------------------
 
 int decode_max_experts() { return kDecMaxExperts; }
@@ -1056,7 +580,12 @@ static bool dec_attr_n() {
          dec_attr<T, kModeG2MN, N>() && dec_attr<T, kModeG2K, N>();
 }
 
-
+bool decode_set_attributes() {
+  bool ok = dec_attr_n<__nv_bfloat16, 16>() && dec_attr_n<__nv_bfloat16, 32>() &&
+            dec_attr_n<__nv_bfloat16, 64>();
+  ok &= dec_attr_n<__half, 16>() && dec_attr_n<__half, 32>() && dec_attr_n<__half, 64>();
+  return ok;
+}
 
 // Launch with the programmatic-serialization attribute: the kernel may start before the
 // previous kernel in the stream completes (the kernels wait with griddepcontrol.wait before
@@ -1098,88 +627,6 @@ static int dec_launch_t(int mode, int n, const CUtensorMap& a0, const CUtensorMa
   if (n == 16) return dec_launch_n<T, 16>(mode, a0, a1, p, grid, s);
   if (n == 32) return dec_launch_n<T, 32>(mode, a0, a1, p, grid, s);
   if (n == 64) return dec_launch_n<T, 64>(mode, a0, a1, p, grid, s);
-  return 1;
-}
-
-template <typename T, int MODE1, int MODE2, int N>
-static size_t dec_one_smem(int num_experts) {
-  using O = DecOneCfg<MODE1, MODE2, N>;
-  return static_cast<size_t>(O::kStages) * O::kStageBytes + 1024 +
-         static_cast<size_t>(2 * num_experts + 2) * sizeof(int32_t);
-}
-
-template <typename T, int MODE1, int MODE2, int N>
-static bool dec_one_attr() {
-  return cudaFuncSetAttribute(decode_ffn_one_kernel<T, MODE1, MODE2, N>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(dec_one_smem<T, MODE1, MODE2, N>(
-                                  kDecMaxExperts))) == cudaSuccess;
-}
-
-template <typename T>
-static bool dec_one_attr_t() {
-  return dec_one_attr<T, kModeG1Dual, kModeG2MN, 16>() &&
-         dec_one_attr<T, kModeG1Dual, kModeG2MN, 32>() &&
-         dec_one_attr<T, kModeG1Dual, kModeG2MN, 64>() &&
-         dec_one_attr<T, kModeG1Single, kModeG2K, 16>() &&
-         dec_one_attr<T, kModeG1Single, kModeG2K, 32>() &&
-         dec_one_attr<T, kModeG1Single, kModeG2K, 64>();
-}
-
-// Cooperative launch: every CTA resident, as GEMM-2's per-chunk waits need.
-template <typename T, int MODE1, int MODE2, int N>
-static int dec_one_launch(const CUtensorMap& g, const CUtensorMap& u, const CUtensorMap& w2,
-                          const DecodeOneParams& p, int grid, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kDecThreads);
-  cfg.dynamicSmemBytes = dec_one_smem<T, MODE1, MODE2, N>(p.E);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, decode_ffn_one_kernel<T, MODE1, MODE2, N>, g, u, w2, p) !=
-      cudaSuccess) {
-    cudaGetLastError();
-    return 4;
-  }
-  return 0;
-}
-
-template <typename T>
-static int dec_one_launch_t(int moe_type, int n, const CUtensorMap& g, const CUtensorMap& u,
-                            const CUtensorMap& w2, const DecodeOneParams& p, int grid,
-                            cudaStream_t s) {
-  if (moe_type == 0) {
-    if (n == 16) return dec_one_launch<T, kModeG1Dual, kModeG2MN, 16>(g, u, w2, p, grid, s);
-    if (n == 32) return dec_one_launch<T, kModeG1Dual, kModeG2MN, 32>(g, u, w2, p, grid, s);
-    if (n == 64) return dec_one_launch<T, kModeG1Dual, kModeG2MN, 64>(g, u, w2, p, grid, s);
-  } else {
-    if (n == 16) return dec_one_launch<T, kModeG1Single, kModeG2K, 16>(g, u, w2, p, grid, s);
-    if (n == 32) return dec_one_launch<T, kModeG1Single, kModeG2K, 32>(g, u, w2, p, grid, s);
-    if (n == 64) return dec_one_launch<T, kModeG1Single, kModeG2K, 64>(g, u, w2, p, grid, s);
-  }
-  return 1;
-}
-
-bool decode_set_attributes() {
-  bool ok = dec_attr_n<__nv_bfloat16, 16>() && dec_attr_n<__nv_bfloat16, 32>() &&
-            dec_attr_n<__nv_bfloat16, 64>();
-  ok &= dec_attr_n<__half, 16>() && dec_attr_n<__half, 32>() && dec_attr_n<__half, 64>();
-  ok &= dec_one_attr_t<__nv_bfloat16>() && dec_one_attr_t<__half>();
-  return ok;
-}
-
-// Both GEMMs in one cooperative launch.  0 on success; 1 unsupported shape; 3 grid; 4 the
-// launch was refused (e.g. not every CTA could be resident): the caller takes the two kernels.
-int launch_decode_one(int dtype, int moe_type, int n, const CUtensorMap& g, const CUtensorMap& u,
-                      const CUtensorMap& w2, const DecodeOneParams& p, int grid, cudaStream_t s) {
-  if (grid <= 0 || grid > kDecMaxGrid || p.E > kDecMaxExperts) return 3;
-  if (p.H % kDecM != 0 || p.I % kDecM != 0) return 1;
-  if (dtype == kBF16) return dec_one_launch_t<__nv_bfloat16>(moe_type, n, g, u, w2, p, grid, s);
-  if (dtype == kF16) return dec_one_launch_t<__half>(moe_type, n, g, u, w2, p, grid, s);
   return 1;
 }
 

@@ -253,14 +253,6 @@ int32_t moe_set_gemm_path(int32_t path);
  */
 int32_t moe_set_sm_reserve(int32_t sms);
 
-/*
- * Decode kernels (calls of at most 32 tokens): 1 (default) runs GEMM-1 and GEMM-2 in one
- * cooperative kernel, GEMM-2 starting on a chunk as soon as that chunk's intermediate rows are
- * final; 0 runs them as two kernels.  Where the cooperative launch is refused the two kernels
- * run.  Process-wide; returns the previous value (-1 for anything but 0 or 1).
- */
-int32_t moe_set_decode_fused(int32_t enable);
-
 /* Which family served the last moe_fused_v2 / fused_moe call of this thread: 1 SIMT, 2 tensor-core
  * grouped GEMMs, 3 tensor-core decode kernels, 0 none. */
 int32_t moe_last_gemm_path(void);
