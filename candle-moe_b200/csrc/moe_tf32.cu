@@ -15,10 +15,13 @@
 //               the K-major B of h.U^T), and GEMM-2's A (contiguous intermediate rows)
 //   warps 2-3   GEMM-1's A: the 128 gathered token rows, 16-byte cp.async copies written into
 //               the 128-byte-swizzled K-major layout; warp 2 also owns the TMEM allocation
-//   warps 8-11  the split: once a stage has landed, each thread rewrites its 16-byte chunks as
-//               hi in place and writes lo to the stage's lo half (same offsets, so the same
-//               swizzle), then orders those writes before the tensor core's reads
-//               (fence.proxy.async) and its warp arrives on the stage's split barrier
+//   warps 8-11  the split: once a stage has landed, each thread reads its 16-byte chunks and
+//               writes lo = v - hi to the stage's lo half (same offsets, so the same swizzle),
+//               then orders those writes before the tensor core's reads (fence.proxy.async) and
+//               its warp arrives on the stage's split barrier.  hi stays the raw f32 value: the
+//               TF32 MMA reads an f32 operand as its 13 low mantissa bits cleared (outputs
+//               bit-identical to writing the cleared values, checked at config 2), so only lo is
+//               written
 //   warp 1      MMA issuer (one thread): per 8-deep K step hi.hi, hi.lo, lo.hi (M = 128, N = 64
 //               or 128), commit to the stage-empty and accumulator-full barriers
 //   warps 4-7   epilogue: TMEM -> registers (one lane per row), activation or routing weight in
@@ -85,7 +88,8 @@ __device__ __forceinline__ uint64_t umma_sdesc_mn32(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// hi (13 low mantissa bits cleared) and lo = v - hi of four values
+// hi (13 low mantissa bits cleared) and lo = v - hi of four values (hi is what the MMA reads
+// from the raw value)
 __device__ __forceinline__ void split4(const uint4& v, uint4& hi, uint4& lo) {
   hi.x = v.x & 0xFFFFE000u;
   hi.y = v.y & 0xFFFFE000u;
@@ -335,14 +339,12 @@ __global__ void __launch_bounds__(kXThreads, 1)
         for (int i = t; i < kAChunks; i += 128) {
           uint4 hi, lo;
           split4(lds128(a_hi + i * 16), hi, lo);
-          sts128(a_hi + i * 16, hi);
           sts128(a_hi + kXAHalf + i * 16, lo);
         }
 #pragma unroll 4
         for (int i = t; i < kBChunks; i += 128) {
           uint4 hi, lo;
           split4(lds128(b_hi + i * 16), hi, lo);
-          sts128(b_hi + i * 16, hi);
           sts128(b_hi + C::kBHalf + i * 16, lo);
         }
         fence_proxy_async_smem();
