@@ -216,7 +216,8 @@ def run_ours(args, world, rank, local):
         import expert_parallel
         layer = expert_parallel.ExpertParallelMoE(E, k, candle_moe.Activation(act),
                                                   mode=args.ep_mode, transport=args.ep_transport,
-                                                  chunks=args.ep_chunks)
+                                                  chunks=args.ep_chunks,
+                                                  compute_groups=args.ep_groups)
         if args.sm_reserve >= 0:
             layer.sm_reserve = args.sm_reserve
         inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
@@ -733,6 +734,9 @@ def main():
                     help="expert-parallel row exchange into peer-mapped landing buffers by SM "
                          "stores fused with pack / slot sum (push) or by copy engines (copy), "
                          "or NCCL all_to_all_single (collective)")
+    ap.add_argument("--ep-groups", type=lambda v: [int(a) for a in v.split(",")], default=None,
+                    help="expert parallelism: chunks computed per fused call, e.g. 1,3,3,1 "
+                         "(sums to --ep-chunks; default one chunk per call)")
     ap.add_argument("--ep-chunks", type=int, default=4,
                     help="expert-parallel token chunks pipelined through dispatch/compute/return")
     ap.add_argument("--sm-reserve", type=int, default=-1,

@@ -457,10 +457,12 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
       const int64_t tiles = mtile_bound * p.n_tiles;
       const int sms = gemm_sms(ds);
       bool done = false;
-      if (g_gemm_path.load() != 3 && !scatter && mode2 == kModeG2MN && bn2 == 256) {
+      if (g_gemm_path.load() != 3 && (!scatter || g_sm_reserve.load() == 0) &&
+          mode2 == kModeG2MN && bn2 == 256) {
         // CTA pairs (cta_group::2): tiles of 256 rows, static schedule; shapes it does not take
-        // fall through to the one-CTA kernel, which also serves the scatter calls of the
-        // expert-parallel layer
+        // fall through to the one-CTA kernel, which also serves the scatter calls that leave
+        // SMs to other kernels (the collective exchange: a static schedule would wait for CTAs
+        // held back by them, where the one-CTA kernel's dynamic one does not)
         const int64_t pair_tiles = (rows / 256 + (E < rows ? E : rows)) * p.n_tiles;
         const int pairs = static_cast<int>(std::min<int64_t>(pair_tiles, pair_grid(ds, sms)));
         done = launch_sm100_gemm2_pair(static_cast<int>(dtype), mA, mB0, p, pairs, stream) == 0;

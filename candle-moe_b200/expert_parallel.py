@@ -46,7 +46,7 @@ default ops are the CUDA library's, which have no CPU fallback.
 """
 from __future__ import annotations
 
-from typing import Optional
+from typing import Optional, Sequence
 
 import numpy as np
 import torch
@@ -292,7 +292,8 @@ class ExpertParallelMoE:
     def __init__(self, num_experts: int, num_selected_experts: int,
                  activation=candle_moe.Activation.Silu, group: Optional[dist.ProcessGroup] = None,
                  ops=None, chunks: int = 4, sm_reserve: int = 24, mode: str = "partials",
-                 transport: str = "auto", wait_timeout_s: float = 5.0):
+                 transport: str = "auto", wait_timeout_s: float = 5.0,
+                 compute_groups: Optional[Sequence[int]] = None):
         self.num_experts = num_experts
         self.k = num_selected_experts
         self.activation = int(activation)
@@ -305,6 +306,14 @@ class ExpertParallelMoE:
         self.num_local = self.end - self.start
         self.ops = ops or CudaOps()
         self.chunks = max(1, chunks)
+        # Landing-buffer transports: consecutive chunks computed as one fused call once the
+        # group's last chunk has landed (sizes in chunks, summing to `chunks`; default one chunk
+        # per call).  Small first and last groups start the GEMMs early and keep the last
+        # return short; larger middle groups pay the per-call costs fewer times.
+        groups = list(compute_groups) if compute_groups else [1] * self.chunks
+        if sum(groups) != self.chunks or min(groups) < 1:
+            raise ValueError(f"compute_groups {groups} must be positive and sum to {self.chunks}")
+        self.compute_groups = groups
         # SMs the expert GEMMs leave to NCCL's kernels while the collective exchange is in
         # flight: the GEMMs are persistent (one CTA per SM), and without free SMs the collectives
         # would only run between GEMM launches.  The GEMMs take tiles dynamically, so the reserve
@@ -530,17 +539,21 @@ class ExpertParallelMoE:
                 ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
                 self._point(f"sent{c}", sig_s)
 
-        # 4. per chunk: wait for the rows, run the local experts, send the results back
+        # 4. per group of chunks: wait for the rows, run the local experts, send the results back
         keep = []
         received = computed = 0
         rows0, meta0, back0, _ = regions[me]
-        for c in range(C):
+        c_first = 0
+        for gsize in self.compute_groups:
+            cs = list(range(c_first, c_first + gsize))
+            c_first += gsize
+            c = cs[-1]
             ops.peer_wait(L.addr[me], G, ep_d + c + 1, self.wait_timeout_s, compute)
             self._point(f"landed{c}")
-            R = int(pairs[:, c, me].sum())
-            r0 = int(recv_start[me, c, 0])
+            R = int(pairs[:, cs, me].sum())
+            r0 = int(recv_start[me, cs[0], 0])
             received += R
-            n_out = int(back[:, c, me].sum())
+            n_out = int(back[:, cs, me].sum())
             computed += n_out
             if R == 0:
                 continue
@@ -548,7 +561,7 @@ class ExpertParallelMoE:
             rm = L.local[meta0 + r0 * meta_b: meta0 + (r0 + R) * meta_b].view(torch.int32) \
                 .view(R, 2 * k)
             e_loc, w_loc, valid, out_row = self._local_experts(rx, rm)
-            n_asg = int(allc[:, c, me, 2].sum())
+            n_asg = int(allc[:, cs, me, 2].sum())
             contrib = torch.empty((n_asg, H), dtype=x.dtype, device=dev)
             if n_asg:
                 ops.local_experts_scatter(rx, gate_local, up_local, down_local, w_loc, e_loc,
@@ -560,14 +573,14 @@ class ExpertParallelMoE:
             else:
                 seg = torch.zeros((R + 1,), dtype=torch.int64, device=dev)
                 torch.cumsum(valid.sum(dim=1), 0, out=seg[1:])
-            dst = [L.addr[s] + regions[s][2] + int(back_start[s, c, me]) * row_b
-                   for s in range(G)]
-            first = [int(v) for v in y_start[me, c]] + [n_out]
-            if push and c == C - 1:
+            if push and gsize == 1 and c == C - 1:
                 # the last chunk has the GPU to itself: slot sum fused with the return, the
                 # partials stored straight into the origins' buffers.  (Earlier chunks sum on
                 # this stream and return by copy engine: a slot sum beside the next chunk's GEMMs
                 # streams its rows through L2 and slows them more than it saves.)
+                dst = [L.addr[s] + regions[s][2] + int(back_start[s, c, me]) * row_b
+                       for s in range(G)]
+                first = [int(v) for v in y_start[me, c]] + [n_out]
                 keep += [contrib, seg]
                 ops.segment_sum_push(contrib, seg, dst, first, compute, 4 * sms)
                 self._point(f"computed{c}")
@@ -577,12 +590,17 @@ class ExpertParallelMoE:
             self._point(f"computed{c}")
             ev_y = ops.record(compute)
             y_addr = y.data_ptr()
-            for j in range(G):
-                s = (me + j) % G
-                n = first[s + 1] - first[s]
-                if n:
-                    ops.wait(copy_s[s], ev_y)
-                    ops.copy_async(dst[s], y_addr + first[s] * row_b, n * row_b, copy_s[s])
+            base = 0  # the group's results: chunk by chunk, each chunk's rows ordered by origin
+            for cc in cs:
+                first = [int(v) for v in y_start[me, cc]] + [int(back[:, cc, me].sum())]
+                for j in range(G):
+                    s = (me + j) % G
+                    n = first[s + 1] - first[s]
+                    if n:
+                        ops.wait(copy_s[s], ev_y)
+                        ops.copy_async(L.addr[s] + regions[s][2] + int(back_start[s, cc, me]) * row_b,
+                                       y_addr + (base + first[s]) * row_b, n * row_b, copy_s[s])
+                base += first[G]
         for s in copy_s + [compute]:
             ops.wait(sig_s, ops.record(s))
         ops.peer_signal(flag_r, ep_r + 1, sig_s)

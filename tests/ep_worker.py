@@ -236,7 +236,7 @@ class CpuOracleOps:
 
 
 def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
-             transport="collective", sizes=None):
+             transport="collective", sizes=None, chunks=3, groups=None):
     """One CPU rank: forward the rank's tokens (the first n of its T for each n in `sizes`, in
     order, through one layer) and report the worst error against the single-process oracle."""
     import expert_parallel
@@ -249,8 +249,9 @@ def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
         case["idx"][::11, -1] = E  # an out-of-range id: skipped everywhere
         e0, e1 = expert_parallel.expert_range(E, world, rank)
         expert_parallel._Landing.SLACK_ROWS = 0  # let a larger second forward grow the buffers
-        layer = expert_parallel.ExpertParallelMoE(E, k, 0, ops=CpuOracleOps(), chunks=3,
-                                                  mode=mode, transport=transport)
+        layer = expert_parallel.ExpertParallelMoE(E, k, 0, ops=CpuOracleOps(), chunks=chunks,
+                                                  mode=mode, transport=transport,
+                                                  compute_groups=groups)
         worst = 0.0
         for n in sizes or [T]:
             lo, hi = rank * T, rank * T + n

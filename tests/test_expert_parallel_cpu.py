@@ -14,12 +14,13 @@ import torch.multiprocessing as mp
 import ep_worker
 
 
-def _run(moe_type, mode, transport, sizes=None, T=40):
+def _run(moe_type, mode, transport, sizes=None, T=40, chunks=3, groups=None):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = ep_worker.free_port()
     procs = [ctx.Process(target=ep_worker.cpu_rank,
-                         args=(r, 2, port, T, 32, 48, 8, 3, moe_type, q, mode, transport, sizes))
+                         args=(r, 2, port, T, 32, 48, 8, 3, moe_type, q, mode, transport, sizes,
+                               chunks, groups))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -36,6 +37,17 @@ def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode, transpor
     for rank, maxdiff, stats in _run(moe_type, mode, transport):
         assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
         assert stats["pairs_sent"] > 0 and stats["rows_received"] > 0
+
+
+@pytest.mark.parametrize("transport", ["copy", "push"])
+@pytest.mark.parametrize("mode", ["exact", "partials"])
+@pytest.mark.parametrize("groups", [(1, 3, 1), (2, 3), (5,)])
+def test_chunks_computed_in_groups(groups, mode, transport):
+    """Five dispatch chunks computed as groups of consecutive chunks (one fused call per group,
+    results returned chunk by chunk): the same outputs as one call per chunk."""
+    for rank, maxdiff, stats in _run(1, mode, transport, sizes=[40, 9], chunks=5, groups=groups):
+        assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
+        assert stats["chunks"] == 5
 
 
 @pytest.mark.parametrize("transport", ["copy", "push"])
