@@ -312,16 +312,13 @@ int fused_impl(const void* input, const void* gate, const void* up, const void* 
   if (ev) cudaEventRecord(ev[0], stream);
   int64_t launches = route_prep_scratch_bytes(rows, E) ? 3 : 1;
 
-  if (dec_n) {
-    // the decode kernels' counters, zeroed before the route preparation so that GEMM-1 follows
-    // it directly (it is launched as the route preparation's programmatic dependent)
-    const size_t ncnt = 4 * static_cast<size_t>(L.dec_units1 + L.dec_units2 + H / 128);
-    if (cudaMemsetAsync(ws + L.dec_cnt, 0, ncnt * sizeof(uint32_t), stream) != cudaSuccess)
-      st = MOE_ERR_CUDA;
-  }
+  // the decode kernels' counters are cleared by the route preparation itself, so that GEMM-1
+  // follows it directly (it is launched as the route preparation's programmatic dependent)
+  const int64_t dec_ncnt = dec_n ? 4 * (L.dec_units1 + L.dec_units2 + H / 128) : 0;
   if (st == MOE_OK)
     st = launch_route_prep(idx, rw, T, k, E, bm, offsets, tile_prefix, s_token, s_w, s_flat,
-                           prep_scratch, stream) == 0
+                           prep_scratch, stream,
+                           reinterpret_cast<uint32_t*>(ws + L.dec_cnt), dec_ncnt) == 0
              ? MOE_OK
              : MOE_ERR_UNSUPPORTED;
   if (st == MOE_OK && k == 1 && !scatter && !dec_n)

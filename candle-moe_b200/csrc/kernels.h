@@ -34,9 +34,11 @@ int launch_router_project(int dtype, int E, const CUtensorMap& x, const CUtensor
 size_t route_prep_scratch_bytes(int64_t rows, int E);
 int route_prep_max_experts();
 bool route_prep_set_attributes();
+// zero / zero_n: words cleared before the tables are complete (the decode kernels' counters).
 int launch_route_prep(const uint32_t* idx, const float* wts, int64_t num_tokens, int k, int E,
                       int bm, int32_t* offsets, int32_t* tile_prefix, int32_t* s_token,
-                      float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream);
+                      float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream,
+                      uint32_t* zero = nullptr, int64_t zero_n = 0);
 
 // ---- moe_simt.cu -----------------------------------------------------------------------------
 struct SimtParams {

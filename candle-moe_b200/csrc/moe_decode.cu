@@ -193,35 +193,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int KB = p.K / kDecK;
   const int G = static_cast<int>(gridDim.x);
 
-  // GEMM-1 waits for the route preparation's tables, then lets GEMM-2 launch: GEMM-2's CTAs
-  // take the SMs' free shared memory, set up and stream their first weight tiles while GEMM-1
-  // finishes (GEMM-2 reads the tables, complete by then, at once, and waits for GEMM-1's
-  // intermediate rows before it reads them).
-  if (C::kG1) {
-    pdl_wait();
-    if (threadIdx.x == 0) pdl_launch_dependents();
-  }
-  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
-    s_cp[i] = __ldg(p.chunk_prefix + i);
-    s_off[i] = __ldg(p.offsets + i);
-  }
-  __syncthreads();
-  const int chunks = s_cp[E];
-  if (chunks == 0) {
-    // no routed row at all: GEMM-2 still owes the caller an output of zeros
-    if (!C::kG1) {
-      T* out = static_cast<T*>(p.final_out);
-      const int64_t n = static_cast<int64_t>(p.num_tokens) * p.M;
-      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-           i += static_cast<int64_t>(G) * blockDim.x)
-        out[i] = Elem<T>::from_f(0.f);
-    }
-    return;
-  }
-  const int64_t U = static_cast<int64_t>(chunks) * MT;
-  int64_t W = 0;  // k-blocks of the stream-K part
-  const DecWork work0 = dec_work(U, KB, G, static_cast<int>(blockIdx.x), &W);
-
+  // Set-up that reads nothing the previous kernels write (barriers, descriptors, TMEM) runs
+  // before the wait, so that it overlaps the route preparation, which lets GEMM-1 launch early.
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_addr(&bar_full[s]), C::kFullCount);
@@ -246,6 +219,39 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem;
+
+  // GEMM-1 waits for the route preparation's tables, then lets GEMM-2 launch: GEMM-2's CTAs
+  // take the SMs' free shared memory, set up and stream their first weight tiles while GEMM-1
+  // finishes (GEMM-2 reads the tables, complete by then, at once, and waits for GEMM-1's
+  // intermediate rows before it reads them).
+  if (C::kG1) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_launch_dependents();
+  }
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_cp[i] = __ldg(p.chunk_prefix + i);
+    s_off[i] = __ldg(p.offsets + i);
+  }
+  __syncthreads();
+  const int chunks = s_cp[E];
+  if (chunks == 0) {
+    // no routed row at all: GEMM-2 still owes the caller an output of zeros
+    if (!C::kG1) {
+      T* out = static_cast<T*>(p.final_out);
+      const int64_t n = static_cast<int64_t>(p.num_tokens) * p.M;
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+           i += static_cast<int64_t>(G) * blockDim.x)
+        out[i] = Elem<T>::from_f(0.f);
+    }
+    if (warp == 2) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+    return;
+  }
+  const int64_t U = static_cast<int64_t>(chunks) * MT;
+  int64_t W = 0;  // k-blocks of the stream-K part
+  const DecWork work0 = dec_work(U, KB, G, static_cast<int>(blockIdx.x), &W);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (weights)

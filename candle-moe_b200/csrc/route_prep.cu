@@ -132,10 +132,18 @@ __device__ __forceinline__ void prep_scan_experts(const int* s_cnt, int E, int b
 }
 
 // ---- small inputs: everything in one CTA --------------------------------------------------
+// Launched as a programmatic dependent: it waits for the previous kernel (the router, whose
+// picks it reads) and at once lets the next one launch, which waits in turn for this kernel's
+// completion before it reads the tables.  `zero` / `zero_n`: words to clear for the next kernels
+// (the decode kernels' counters), in place of a separate memset.
 __global__ void __launch_bounds__(kPrepThreads) route_prep_single_kernel(
     const uint32_t* __restrict__ idx, const float* __restrict__ wts, int64_t rows, int k, int E,
     int bm, int32_t* __restrict__ offsets, int32_t* __restrict__ tile_prefix,
-    int32_t* __restrict__ s_token, float* __restrict__ s_weight, int32_t* __restrict__ s_flat) {
+    int32_t* __restrict__ s_token, float* __restrict__ s_weight, int32_t* __restrict__ s_flat,
+    uint32_t* __restrict__ zero, int64_t zero_n) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int64_t i = threadIdx.x; i < zero_n; i += blockDim.x) zero[i] = 0u;
   extern __shared__ int smem_i[];
   int* s_cnt = smem_i;
   int* s_run = smem_i + E;
@@ -228,16 +236,29 @@ bool route_prep_set_attributes() {
 // scratch: route_prep_scratch_bytes() bytes (may be null when that is 0).
 int launch_route_prep(const uint32_t* idx, const float* wts, int64_t num_tokens, int k, int E,
                       int bm, int32_t* offsets, int32_t* tile_prefix, int32_t* s_token,
-                      float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream) {
+                      float* s_weight, int32_t* s_flat, void* scratch, cudaStream_t stream,
+                      uint32_t* zero, int64_t zero_n) {
   if (E < 1 || E > route_prep_max_experts() || k < 1 || bm < 1) return 1;
   const int64_t rows = num_tokens * k;
   const int64_t nb = (rows + kPrepRows - 1) / kPrepRows;
   if (nb <= 1) {
-    const size_t smem = static_cast<size_t>(2 * E + kPrepWarps * E) * sizeof(int);
-    route_prep_single_kernel<<<1, kPrepThreads, smem, stream>>>(idx, wts, rows, k, E, bm, offsets,
-                                                                tile_prefix, s_token, s_weight, s_flat);
-    return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kPrepThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(2 * E + kPrepWarps * E) * sizeof(int);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, route_prep_single_kernel, idx, wts, rows, k, E, bm, offsets,
+                              tile_prefix, s_token, s_weight, s_flat, zero, zero_n) == cudaSuccess
+               ? 0
+               : 1;
   }
+  if (zero_n > 0 && cudaMemsetAsync(zero, 0, sizeof(uint32_t) * zero_n, stream) != cudaSuccess)
+    return 1;
   if (nb > 0x7fffffff / E) return 1;
   int32_t* counts = static_cast<int32_t*>(scratch);
   int32_t* base = counts + nb * E;

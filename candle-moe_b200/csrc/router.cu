@@ -44,6 +44,9 @@ template <int E, int KC>
 __global__ void __launch_bounds__(256) router_topk_softmax_kernel(
     const float* __restrict__ logits, float* __restrict__ out_w, int32_t* __restrict__ out_idx,
     int32_t* __restrict__ out_src, int num_tokens, int k_arg, int renorm) {
+  // a kernel launched after this one as its programmatic dependent (the route preparation) may
+  // start now; it waits for this kernel's completion before it reads the picks
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int k = KC > 0 ? KC : k_arg;
   using G = RouterGeom<E>;
   constexpr int kElts = G::kElts, kVpt = G::kVpt, kTpr = G::kTpr, kVecs = G::kVecs;
