@@ -143,10 +143,8 @@ __global__ void __launch_bounds__(kXThreads, 1)
   const int E = p.E;
   const int num_kb = p.K / kXBK;
 
-  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
-    s_tp[i] = __ldg(p.tile_prefix + i);
-    s_off[i] = __ldg(p.offsets + i);
-  }
+  // Launched as a programmatic dependent: the set-up below reads nothing the previous kernels
+  // write and overlaps their end; the tables and operands are read after the wait.
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_addr(&bar_full[s]), C::kFullCount);
@@ -173,6 +171,13 @@ __global__ void __launch_bounds__(kXThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    s_tp[i] = __ldg(p.tile_prefix + i);
+    s_off[i] = __ldg(p.offsets + i);
+  }
+  __syncthreads();
   const int total_tiles = s_tp[E] * p.n_tiles;
   const int G = static_cast<int>(gridDim.x);
 
@@ -465,8 +470,21 @@ int x_launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
              const Sm100Params& p, int grid, cudaStream_t s) {
   const size_t smem = x_smem<MODE, BN>(p.E);
   if (smem > kXSmemMax) return 2;
-  tf32x3_grouped_gemm_kernel<MODE, BN><<<grid, kXThreads, smem, s>>>(a, b0, b1, p);
-  return 0;
+  // programmatic dependent of the previous kernel (the route preparation or GEMM-1)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kXThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tf32x3_grouped_gemm_kernel<MODE, BN>, a, b0, b1, p) ==
+                 cudaSuccess
+             ? 0
+             : 4;
 }
 
 }  // namespace
