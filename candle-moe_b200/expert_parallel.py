@@ -26,8 +26,9 @@ mapped by every other rank; every offset follows from the all-gathered count mat
 (p2p_layout), so each rank computes the same layout, and buffers grow collectively when a rank's
 need exceeds its capacity.  After a chunk's rows are in place the sender release-stores the
 chunk's epoch into the destination's flag for this sender (moe_peer_signal); the destination's
-compute stream waits for all senders' flags with a bounded wait (moe_peer_wait) before its GEMMs
-read the rows.
+compute stream waits for the other senders' flags with a bounded wait (moe_peer_wait) and for its
+own rows by stream order (an event of the side stream that wrote them), so no kernel polls a flag
+that another kernel of the same GPU writes, before its GEMMs read the rows.
 
   "push" (default on GPUs): SM stores over NVLink, fused with the kernels that produce the rows:
     moe_ep_push_pairs writes each pair's token row and metadata straight into the destination's
@@ -439,6 +440,17 @@ class ExpertParallelMoE:
         return self._forward_collective(x, gate_local, up_local, down_local, routing_weights,
                                         expert_indices, moe_type)
 
+    def _wait_others(self, flags, value, stream, ev_own):
+        """Stream-ordered arrival wait: a bounded poll of the flags the other ranks write (their
+        GPUs run their kernels), and an event for this rank's own contribution, which its own
+        side stream produced -- no kernel of this GPU spins on another kernel of the same GPU."""
+        ops, G, me = self.ops, self.world, self.rank
+        if me > 0:
+            ops.peer_wait(flags, me, value, self.wait_timeout_s, stream)
+        if me + 1 < G:
+            ops.peer_wait(flags + 4 * (me + 1), G - me - 1, value, self.wait_timeout_s, stream)
+        ops.wait(stream, ev_own)
+
     def _chunking(self, T):
         C = self.chunks  # the same on every rank: the counts exchange has shape [C, G, 3]
         Tc = max(1, (T + C - 1) // C)
@@ -502,6 +514,7 @@ class ExpertParallelMoE:
         flag_r = [L.addr[r] + 4 * (G + me) for r in range(G)]
         ep_d, ep_r = L.epoch_dispatch, L.epoch_return
         ev_ready = ops.record(compute)
+        ev_sent = []  # per chunk: this rank's own rows are in its buffer (stream order)
         if push:
             # fused pack + dispatch: SM stores straight into the destinations' landing rows; the
             # first chunk has the GPU to itself, later ones share it with the GEMMs
@@ -516,6 +529,7 @@ class ExpertParallelMoE:
                     ops.push_pairs(x, p_tok, p_flat, off, c, idx, w, E, G, rows_to, meta_to,
                                    sig_s, 4 * sms if c == 0 else sms)
                 ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
+                ev_sent.append(ops.record(sig_s))
                 self._point(f"sent{c}", sig_s)
         else:
             # copy engines, one stream per destination
@@ -537,6 +551,7 @@ class ExpertParallelMoE:
                 for s in copy_s:
                     ops.wait(sig_s, ops.record(s))
                 ops.peer_signal(flag_d, ep_d + c + 1, sig_s)
+                ev_sent.append(ops.record(sig_s))
                 self._point(f"sent{c}", sig_s)
 
         # 4. per group of chunks: wait for the rows, run the local experts, send the results back
@@ -548,7 +563,7 @@ class ExpertParallelMoE:
             cs = list(range(c_first, c_first + gsize))
             c_first += gsize
             c = cs[-1]
-            ops.peer_wait(L.addr[me], G, ep_d + c + 1, self.wait_timeout_s, compute)
+            self._wait_others(L.addr[me], ep_d + c + 1, compute, ev_sent[c])
             self._point(f"landed{c}")
             R = int(pairs[:, cs, me].sum())
             r0 = int(recv_start[me, cs[0], 0])
@@ -604,8 +619,9 @@ class ExpertParallelMoE:
         for s in copy_s + [compute]:
             ops.wait(sig_s, ops.record(s))
         ops.peer_signal(flag_r, ep_r + 1, sig_s)
+        ev_back = ops.record(sig_s)
         self._point("returned", sig_s)
-        ops.peer_wait(L.addr[me] + 4 * G, G, ep_r + 1, self.wait_timeout_s, compute)
+        self._wait_others(L.addr[me] + 4 * G, ep_r + 1, compute, ev_back)
         self._point("all_returned")
         L.epoch_dispatch, L.epoch_return = ep_d + C, ep_r + 1
         self._mark()
