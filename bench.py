@@ -221,6 +221,27 @@ def run_ours(args, world, rank, local):
         if args.sm_reserve >= 0:
             layer.sm_reserve = args.sm_reserve
         inp = make_inputs(cfg, seed=0, rank=rank, n_local_experts=layer.num_local)
+        if args.ep_balance:
+            # expert placement from the router's loads over every rank's tokens (16 experts per
+            # GPU at 8 GPUs either way); the synthetic weights stand for the placed experts
+            import torch.distributed as dist
+            _, idx0, _ = candle_moe.topk_softmax(inp["logits"], k, renormalize=renorm)
+            loads = torch.bincount(idx0.long().flatten().clamp(max=E), minlength=E + 1)[:E]
+            dist.all_reduce(loads)
+            loads = loads.tolist()
+            slot = expert_parallel.balanced_placement(loads, world)
+            layer.set_placement(slot)
+            El = E // world
+            per_rank = [0] * world
+            for e in range(E):
+                per_rank[slot[e] // El] += loads[e]
+            contiguous = [sum(loads[r * El:(r + 1) * El]) for r in range(world)]
+            mean = sum(loads) / world
+            ep_placement = {"balanced": True,
+                            "rank_assignments_max_over_mean": round(max(per_rank) / mean, 4),
+                            "contiguous_max_over_mean": round(max(contiguous) / mean, 4)}
+        else:
+            ep_placement = {"balanced": False}
     else:
         inp = make_inputs(cfg, seed=0, rank=rank)
     moe = None if router_only else candle_moe.FusedMoE(E, k, candle_moe.Activation(act))
@@ -370,6 +391,7 @@ def run_ours(args, world, rank, local):
         st, n = layer.stage_times()
         line["ep_stages_ms"] = {s_: v / max(n, 1) for s_, v in st.items()}
         line["ep_rows"] = {k_: int(v) for k_, v in layer.last_stats.items()}
+        line["ep_placement"] = ep_placement
         if layer.transport in ("push", "copy"):
             line["ep_timeline_ms"] = {k_: round(v, 3) for k_, v in layer.timeline().items()}
     if not router_only and ncalls:
@@ -737,6 +759,9 @@ def main():
     ap.add_argument("--ep-groups", type=lambda v: [int(a) for a in v.split(",")], default=None,
                     help="expert parallelism: chunks computed per fused call, e.g. 1,3,3,1 "
                          "(sums to --ep-chunks; default one chunk per call)")
+    ap.add_argument("--ep-balance", action=argparse.BooleanOptionalAction, default=True,
+                    help="expert parallelism: place experts by the router's loads "
+                         "(balanced_placement) instead of contiguous ranges")
     ap.add_argument("--ep-chunks", type=int, default=4,
                     help="expert-parallel token chunks pipelined through dispatch/compute/return")
     ap.add_argument("--sm-reserve", type=int, default=-1,

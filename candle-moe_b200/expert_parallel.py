@@ -56,6 +56,38 @@ import torch.distributed as dist
 import candle_moe
 
 
+def balanced_placement(expert_load, world: int):
+    """Expert placement for load balance: returns slot[e] for each expert e, a permutation of
+    range(E) where rank r owns the experts whose slots lie in [r*E/world, (r+1)*E/world) -- still
+    E/world experts per rank.  Experts in decreasing load go to the rank with the least load so
+    far that still has room (greedy), which evens out the rows each rank computes when the
+    router favours some experts (BASELINE config 5's per-expert bias)."""
+    loads = [float(v) for v in expert_load]
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"num_experts {E} is not divisible by world size {world}")
+    El = E // world
+    rank_load, filled = [0.0] * world, [0] * world
+    slot = [0] * E
+    for e in sorted(range(E), key=lambda e: (-loads[e], e)):
+        r = min((r for r in range(world) if filled[r] < El), key=lambda r: (rank_load[r], r))
+        slot[e] = r * El + filled[r]
+        filled[r] += 1
+        rank_load[r] += loads[e]
+    return slot
+
+
+def local_experts(slot, world: int, rank: int):
+    """Global ids of the experts `rank` owns under placement `slot`, in local-id order (the order
+    in which that rank passes their weights to forward)."""
+    E = len(slot)
+    El = E // world
+    inv = [0] * E
+    for e, sl in enumerate(slot):
+        inv[sl] = e
+    return inv[rank * El:(rank + 1) * El]
+
+
 def expert_range(num_experts: int, world: int, rank: int):
     """Experts [start, end) owned by `rank` (E must divide evenly)."""
     if num_experts % world:
@@ -329,6 +361,8 @@ class ExpertParallelMoE:
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         self.wait_timeout_s = wait_timeout_s
+        self._slot = None            # expert placement (set_placement); None: expert_range
+        self._slot_dev = {}
         self._landing = None
         self._streams = None
         self._zeros = {}
@@ -399,12 +433,31 @@ class ExpertParallelMoE:
             raise TimeoutError(f"expert-parallel exchange: an arrival wait ran out "
                                f"(device error bits {bits:#x})")
 
+    def set_placement(self, slot):
+        """Place experts by `slot` (see balanced_placement): expert e lives on rank
+        slot[e] // (E/world) as local expert slot[e] % (E/world), so each rank passes forward the
+        weights of local_experts(slot, world, rank) in that order.  Every rank must set the same
+        placement; None restores the contiguous ranges of expert_range."""
+        if slot is not None:
+            slot = [int(v) for v in slot]
+            if sorted(slot) != list(range(self.num_experts)):
+                raise ValueError("placement must be a permutation of range(num_experts)")
+        self._slot = slot
+        self._slot_dev = {}
+
     # ---- forward -----------------------------------------------------------------------------
     def _plan(self, x, routing_weights, expert_indices, C, Tc):
         """Pairs sorted by (chunk, rank, token) and the [C, G, 3] counts this rank sends."""
         G, E = self.world, self.num_experts
         dev = x.device
         idx = expert_indices.to(torch.int32).contiguous()
+        if self._slot is not None:
+            # global expert ids -> placement slots; ids outside [0, E) stay as they are (skipped)
+            st = self._slot_dev.get(dev)
+            if st is None:
+                st = self._slot_dev[dev] = torch.tensor(self._slot, dtype=torch.int32, device=dev)
+            valid = (idx >= 0) & (idx < E)
+            idx = torch.where(valid, st[idx.clamp(0, E - 1).long()], idx).contiguous()
         w = routing_weights.contiguous()
         groups, asg = self.ops.dest_groups(idx, E, G, Tc, C)
         zw = self._zeros.get(groups.shape)

@@ -236,7 +236,7 @@ class CpuOracleOps:
 
 
 def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
-             transport="collective", sizes=None, chunks=3, groups=None):
+             transport="collective", sizes=None, chunks=3, groups=None, placement=None):
     """One CPU rank: forward the rank's tokens (the first n of its T for each n in `sizes`, in
     order, through one layer) and report the worst error against the single-process oracle."""
     import expert_parallel
@@ -248,18 +248,22 @@ def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
                         wstd=0.1)
         case["idx"][::11, -1] = E  # an out-of-range id: skipped everywhere
         e0, e1 = expert_parallel.expert_range(E, world, rank)
+        mine = list(range(e0, e1))
         expert_parallel._Landing.SLACK_ROWS = 0  # let a larger second forward grow the buffers
         layer = expert_parallel.ExpertParallelMoE(E, k, 0, ops=CpuOracleOps(), chunks=chunks,
                                                   mode=mode, transport=transport,
                                                   compute_groups=groups)
+        if placement is not None:
+            layer.set_placement(placement)
+            mine = expert_parallel.local_experts(placement, world, rank)
         worst = 0.0
         for n in sizes or [T]:
             lo, hi = rank * T, rank * T + n
             out = layer.forward(torch.from_numpy(case["x"][lo:hi].copy()),
-                                torch.from_numpy(case["gate"][e0:e1].copy()),
-                                torch.from_numpy(case["up"][e0:e1].copy()),
+                                torch.from_numpy(case["gate"][mine].copy()),
+                                torch.from_numpy(case["up"][mine].copy()),
                                 None if case["down"] is None else
-                                torch.from_numpy(case["down"][e0:e1].copy()),
+                                torch.from_numpy(case["down"][mine].copy()),
                                 torch.from_numpy(case["w"][lo:hi].copy()),
                                 torch.from_numpy(case["idx"][lo:hi].copy()), moe_type)
             ref = oracle.moe_forward(case["x"][lo:hi].copy(), case["gate"], case["up"],
@@ -276,7 +280,7 @@ def cpu_rank(rank, world, port, T, H, I, E, k, moe_type, result_q, mode="exact",
 
 
 def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="exact",
-             transport="auto"):
+             transport="auto", balance=False):
     import candle_moe
     import expert_parallel
     from moe_testlib import to_torch
@@ -299,9 +303,17 @@ def gpu_rank(rank, world, port, T, H, I, E, k, moe_type, dtype, result_q, mode="
         w = torch.from_numpy(case["w"]).cuda()
         idx = torch.from_numpy(case["idx"]).cuda()
         layer = expert_parallel.ExpertParallelMoE(E, k, 0, mode=mode, transport=transport)
+        mine = torch.arange(e0, e1, device="cuda")
+        if balance:
+            # placement from the expert loads of all ranks' tokens (the biased router's)
+            loads = torch.bincount(idx.long().flatten().clamp(max=E), minlength=E + 1)[:E]
+            slot = expert_parallel.balanced_placement(loads.tolist(), world)
+            layer.set_placement(slot)
+            mine = torch.tensor(expert_parallel.local_experts(slot, world, rank), device="cuda")
+        Gl, Ul = G[mine].contiguous(), U[mine].contiguous()
+        Dl = None if D is None else D[mine].contiguous()
         for _ in range(2):  # the second forward reuses the landing buffers and flag epochs
-            out = layer.forward(x[lo:hi].contiguous(), G[e0:e1].contiguous(),
-                                U[e0:e1].contiguous(), None if D is None else D[e0:e1].contiguous(),
+            out = layer.forward(x[lo:hi].contiguous(), Gl, Ul, Dl,
                                 w[lo:hi].contiguous(), idx[lo:hi].contiguous(), moe_type)
         ref = candle_moe.FusedMoE(E, k).forward(x[lo:hi].contiguous(), G, U, D,
                                                 w[lo:hi].contiguous(), idx[lo:hi].contiguous(),

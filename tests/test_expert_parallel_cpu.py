@@ -12,15 +12,16 @@ import pytest
 import torch.multiprocessing as mp
 
 import ep_worker
+import expert_parallel
 
 
-def _run(moe_type, mode, transport, sizes=None, T=40, chunks=3, groups=None):
+def _run(moe_type, mode, transport, sizes=None, T=40, chunks=3, groups=None, placement=None):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = ep_worker.free_port()
     procs = [ctx.Process(target=ep_worker.cpu_rank,
                          args=(r, 2, port, T, 32, 48, 8, 3, moe_type, q, mode, transport, sizes,
-                               chunks, groups))
+                               chunks, groups, placement))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -37,6 +38,30 @@ def test_expert_parallel_matches_single_process_on_gloo(moe_type, mode, transpor
     for rank, maxdiff, stats in _run(moe_type, mode, transport):
         assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
         assert stats["pairs_sent"] > 0 and stats["rows_received"] > 0
+
+
+@pytest.mark.parametrize("transport", ["collective", "copy", "push"])
+@pytest.mark.parametrize("mode", ["exact", "partials"])
+def test_expert_placement(mode, transport):
+    """Experts placed by a permutation (rank 0 owns experts 7, 2, 4, 1; rank 1 owns 0, 3, 5, 6):
+    each rank passes its placed experts' weights, and the outputs equal the single-process
+    oracle as with the contiguous ranges."""
+    placement = [4, 3, 1, 5, 2, 6, 7, 0]  # slot of expert e; slots 0-3 on rank 0
+    assert expert_parallel.local_experts(placement, 2, 0) == [7, 2, 4, 1]
+    for rank, maxdiff, stats in _run(0, mode, transport, placement=placement):
+        assert maxdiff == 0.0 if mode == "exact" else maxdiff < 1e-6, (rank, maxdiff)
+
+
+def test_balanced_placement_evens_the_ranks():
+    loads = [100, 90, 80, 70, 60, 50, 40, 30]
+    slot = expert_parallel.balanced_placement(loads, 2)
+    assert sorted(slot) == list(range(8))
+    per_rank = [sum(loads[e] for e in range(8) if slot[e] // 4 == r) for r in range(2)]
+    assert max(per_rank) - min(per_rank) <= 20, per_rank  # contiguous ranges: 340 vs 180
+    loads = [100, 90, 80, 10, 10, 5, 5, 0]  # the best split of four and four is 125 / 175
+    slot = expert_parallel.balanced_placement(loads, 2)
+    per_rank = [sum(loads[e] for e in range(8) if slot[e] // 4 == r) for r in range(2)]
+    assert max(per_rank) == 175, per_rank
 
 
 @pytest.mark.parametrize("transport", ["copy", "push"])
