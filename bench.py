@@ -759,9 +759,10 @@ def main():
     ap.add_argument("--ep-groups", type=lambda v: [int(a) for a in v.split(",")], default=None,
                     help="expert parallelism: chunks computed per fused call, e.g. 1,3,3,1 "
                          "(sums to --ep-chunks; default one chunk per call)")
-    ap.add_argument("--ep-balance", action=argparse.BooleanOptionalAction, default=True,
+    ap.add_argument("--ep-balance", action=argparse.BooleanOptionalAction, default=False,
                     help="expert parallelism: place experts by the router's loads "
-                         "(balanced_placement) instead of contiguous ranges")
+                         "(balanced_placement) instead of contiguous ranges (off by default: "
+                         "the synthetic router's per-rank loads are within 8 %% of even)")
     ap.add_argument("--ep-chunks", type=int, default=4,
                     help="expert-parallel token chunks pipelined through dispatch/compute/return")
     ap.add_argument("--sm-reserve", type=int, default=-1,
